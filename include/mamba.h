@@ -1,0 +1,268 @@
+/*
+ * mamba.h -- C ABI of libmamba_b200.so, the B200 (sm_100a) implementation of
+ * the mamba-metal selective-scan path.
+ *
+ * Part 1 is the reference's C API, symbol for symbol, with the same
+ * signatures, argument meaning and error convention (int 0 = success,
+ * -1 = failure; NULL from the create functions on failure).  It replaces
+ * Sources/Mamba/MambaRuntime.hpp:69-85 of SNAPKITTYWEST/mamba-metal.
+ * Part 2 holds extensions (device-pointer entry points, weight blob helpers,
+ * error text).  Part 3 exposes the individual kernels on device pointers, in
+ * the buffer order of the reference's Metal kernels, for callers that drive
+ * their own layer graph and for the parity tests.
+ *
+ * Pure C: no C++ or PyTorch types cross this boundary.  All "stream"
+ * arguments are cudaStream_t values passed as void*; NULL selects the
+ * model's own stream (Part 1/2) or the legacy default stream (Part 3).
+ */
+#ifndef MAMBA_B200_H
+#define MAMBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Part 1: the reference C API                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Element type.  Replaces enum class DType { F32, F16 }
+ * (Sources/Mamba/MambaConfig.hpp:6); same values. */
+typedef enum MambaDType { MAMBA_F32 = 0, MAMBA_F16 = 1 } MambaDType;
+
+/* Model hyper-parameters.  Layout-compatible with mamba::MambaConfig
+ * (Sources/Mamba/MambaConfig.hpp:8-18): 24 bytes, n_layer at offset 16,
+ * dtype at offset 20.  d_inner = expand * d_model; dt_rank is derived as
+ * ceil(d_model / 16).  dtype selects the activation and GEMM-weight type;
+ * the SSM state is always FP32. */
+typedef struct MambaConfig {
+    int32_t d_model;
+    int32_t d_state; /* N, 1..16 */
+    int32_t d_conv;  /* K, 1..8  */
+    int32_t expand;
+    int32_t n_layer;
+    int32_t dtype; /* MambaDType */
+} MambaConfig;
+
+typedef struct MambaModel MambaModel;             /* MambaRuntime.hpp:71 */
+typedef struct MambaStateHandle MambaStateHandle; /* MambaRuntime.hpp:72 */
+
+/* Replaces mamba_create (MambaRuntime.hpp:74, MambaRuntime.cpp:134-143).
+ * Binds the calling thread's current CUDA device (must be sm_100), creates
+ * the model's stream and allocates zero weights.  NULL on failure. */
+MambaModel *mamba_create(const MambaConfig *cfg);
+
+/* Replaces mamba_destroy (MambaRuntime.hpp:75, MambaRuntime.cpp:145-147).
+ * Does not free state handles (as in the reference); they stay valid. */
+void mamba_destroy(MambaModel *m);
+
+/* Replaces mamba_load_weights (MambaRuntime.hpp:77, stub at
+ * MambaRuntime.cpp:59-67).  Parses the weight blob format documented in
+ * Part 2 (64-byte header, then per-layer FP32 tensors in MambaWeights order,
+ * MambaRuntime.hpp:13-25, plus dt_bias).  0 / -1. */
+int mamba_load_weights(MambaModel *m, const void *data, size_t size);
+
+/* Replaces mamba_forward (MambaRuntime.hpp:78, MambaRuntime.cpp:154-157).
+ * input/output: HOST FP32 [batch, seq_len, d_model].  Runs every layer
+ * (RMSNorm -> in_proj -> causal conv + SiLU -> x_proj -> dt_proj ->
+ * selective scan with SiLU(z) gate -> out_proj + residual) and returns when
+ * the output is in host memory.  input and output may alias.  0 / -1. */
+int mamba_forward(MambaModel *m, const float *input, float *output, int batch, int seq_len);
+
+/* Replaces mamba_create_state (MambaRuntime.hpp:80, MambaRuntime.cpp:69-78).
+ * FP32 conv_state [n_layer, batch, d_inner, d_conv-1] and ssm_state
+ * [n_layer, batch, d_inner, d_state] on the model's device, zeroed. */
+MambaStateHandle *mamba_create_state(MambaModel *m, int batch);
+
+/* Replaces mamba_reset_state (MambaRuntime.hpp:81, MambaRuntime.cpp:80-90). */
+void mamba_reset_state(MambaStateHandle *s);
+
+/* Replaces mamba_step (MambaRuntime.hpp:82, MambaRuntime.cpp:170-173).
+ * token/out: HOST FP32 [batch, d_model] where batch is the state's batch
+ * (the reference drops the batch and steps one row; this implementation
+ * steps every row of the state).  Updates the state in place.  0 / -1. */
+int mamba_step(MambaModel *m, MambaStateHandle *s, const float *token, float *out);
+
+/* Replaces mamba_destroy_state (MambaRuntime.hpp:83, MambaRuntime.cpp:175-177). */
+void mamba_destroy_state(MambaStateHandle *s);
+
+/* ------------------------------------------------------------------------ */
+/* Part 2: extensions                                                       */
+/* ------------------------------------------------------------------------ */
+
+/* Text of the last failure on the calling thread ("" if none).  The
+ * reference only prints to stderr (MambaRuntime.cpp:42,65). */
+const char *mamba_last_error(void);
+
+/* dt_rank used for a config: ceil(d_model / 16). */
+int mamba_dt_rank(const MambaConfig *cfg);
+
+/* Weight blob layout accepted by mamba_load_weights:
+ *   bytes 0..7   magic "MAMBAB2\0"
+ *   bytes 8..11  uint32 version (1)
+ *   bytes 12..15 uint32 header size (64)
+ *   bytes 16..39 MambaConfig (must equal the model's)
+ *   bytes 40..43 int32 dt_rank (must equal mamba_dt_rank)
+ *   bytes 44..63 zero
+ *   then for each layer, FP32 row-major, in this order:
+ *     in_proj [d_model, 2*d_inner], conv1d [d_inner, d_conv],
+ *     conv_bias [d_inner], x_proj [d_inner, dt_rank + 2*d_state],
+ *     dt_proj [dt_rank, d_inner], A [d_inner, d_state] (negative, i.e.
+ *     -exp(A_log)), D [d_inner], out_proj [d_inner, d_model],
+ *     norm_weight [d_model], dt_bias [d_inner]. */
+size_t mamba_weights_blob_size(const MambaConfig *cfg);
+
+/* Fills every weight on the device from a seed (synthetic checkpoints):
+ * linear ~ N(0, 0.02), conv1d and conv_bias ~ U(-0.5, 0.5),
+ * dt_bias = softplus^-1(dt) with dt ~ logU[1e-3, 1e-1],
+ * A[d,n] = -(n+1), D = 1, norm_weight = 1.  0 / -1. */
+int mamba_init_weights_random(MambaModel *m, uint64_t seed);
+
+/* Device-pointer forward: input/output are DEVICE FP32 [batch, seq_len,
+ * d_model] on the model's device (may alias).  Enqueued on `stream` (NULL =
+ * the model's stream); does not synchronize. */
+int mamba_forward_device(MambaModel *m, const float *input, float *output, int batch,
+                         int seq_len, void *stream);
+
+/* Device-pointer decode step: token/out DEVICE FP32 [batch, d_model].
+ * Enqueued on `stream` (NULL = the model's stream); does not synchronize. */
+int mamba_step_device(MambaModel *m, MambaStateHandle *s, const float *token, float *out,
+                      void *stream);
+
+/* Batch of the state handle, or -1. */
+int mamba_state_batch(const MambaStateHandle *s);
+
+/* Device pointers of a state's FP32 buffers for one layer (for export,
+ * import and tests).  0 / -1. */
+int mamba_state_buffers(MambaStateHandle *s, int layer, float **conv_state, float **ssm_state);
+
+/* Use `stream` (a cudaStream_t on the model's device, owned by the caller)
+ * for every later call on this model, including the host-pointer
+ * mamba_forward / mamba_step; NULL returns to the model's own stream. */
+int mamba_set_stream(MambaModel *m, void *stream);
+
+/* Per-operation timing of the layer graph (tracing).  While enabled, the
+ * runtime records a CUDA event pair around every operation it enqueues;
+ * mamba_profile_read sums the event times of one operation over all
+ * recorded calls (waiting for the last event).  Operations: */
+typedef enum MambaOp {
+    MAMBA_OP_RMSNORM = 0,
+    MAMBA_OP_IN_PROJ = 1,
+    MAMBA_OP_CONV = 2,
+    MAMBA_OP_X_PROJ = 3,
+    MAMBA_OP_DT_PROJ = 4,
+    MAMBA_OP_SCAN = 5, /* selective scan (forward) or SSM update (step) */
+    MAMBA_OP_OUT_PROJ = 6,
+    MAMBA_OP_COUNT = 7
+} MambaOp;
+int mamba_profile_enable(MambaModel *m, int on); /* clears the records */
+/* total_ms: summed duration; calls: recorded operations; kernels: kernels
+ * of this library launched by those operations (0 for library GEMMs). */
+int mamba_profile_read(MambaModel *m, int op, double *total_ms, int64_t *calls, int64_t *kernels);
+
+/* ------------------------------------------------------------------------ */
+/* Part 3: kernels on device pointers                                       */
+/* ------------------------------------------------------------------------ */
+
+/* Arguments of the fused selective scan.  Buffer order follows
+ * selective_scan_f32 (Sources/Kernels/selective_scan.metal:84-93: x, delta,
+ * B, C, A, D, y, final_state) with the gate of
+ * fused_selective_scan_gate_f32 (Sources/Kernels/mamba_block.metal:36-45)
+ * and the dims of ScanParams (selective_scan.metal:32-38).
+ * Per (b, t, d):  dt = softplus(delta + dt_bias);
+ *   for n: a = exp(dt*A[d,n]); Bbar = (a-1)/A[d,n]*B  (dt*B when
+ *   |A| <= 1e-6); h = a*h + Bbar*x;  y = sum_n C*h + D*x;
+ *   if z: y *= SiLU(z).   (Sources/CPURef/selective_scan_cpu.cpp:17-41)
+ * Strides are in elements: {batch, time, channel} for x, delta, z, y and
+ * {batch, time, state} for B, C.  dtypes: x, z and y share x_dtype.
+ * Supported (x, delta, B/C): (F32,F32,F32), (F16,F16,F16), (F16,F32,F16),
+ * (F16,F32,F32). */
+typedef struct MambaScanArgs {
+    const void *x;
+    const void *delta;
+    const void *B;
+    const void *C;
+    const float *A;             /* [dim, dstate] */
+    const float *D;             /* [dim] or NULL (no skip term) */
+    void *y;
+    float *final_state;         /* [batch, dim, dstate] or NULL */
+    const void *z;              /* gate or NULL */
+    const float *dt_bias;       /* [dim] or NULL */
+    const float *initial_state; /* [batch, dim, dstate] or NULL (zeros) */
+    int32_t batch, seqlen, dim, dstate;
+    int32_t x_dtype, delta_dtype, bc_dtype;
+    int32_t chunk_len;          /* time chunk per CTA; 0 = automatic */
+    int64_t x_stride[3], delta_stride[3], B_stride[3], C_stride[3], z_stride[3], y_stride[3];
+} MambaScanArgs;
+
+/* Scratch bytes mamba_selective_scan needs for these args (the per-chunk
+ * carries of a sequence split into several time chunks); 0 when the scan
+ * runs as one chunk per channel. */
+size_t mamba_selective_scan_workspace(const MambaScanArgs *a);
+
+/* Fused selective scan (selective_scan.metal:84-244 and
+ * mamba_block.metal:36-128, with the cross-chunk carry that
+ * prefix_scan.metal:19-40 intended).  workspace: device memory of at least
+ * mamba_selective_scan_workspace(a) bytes (may be NULL when that is 0).
+ * 0 / -1 (see mamba_last_error). */
+int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* Sequence-sharded mode, step 1: summary of this rank's slice of the
+ * sequence: for every (b, d, n) the affine map h -> P*h + H that the slice
+ * applies to its incoming state.  P, H: DEVICE FP32 [batch, dim, dstate].
+ * y, z, C and the initial/final state in `a` are ignored. */
+int mamba_scan_summary(const MambaScanArgs *a, float *P, float *H, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/* Sequence-sharded mode, step 2: given the summaries of all ranks gathered
+ * as PH[world][2][count] (P then H, count = batch*dim*dstate), compose the
+ * state entering rank `rank`: h_in = S_{rank-1} o ... o S_0 (h0), with h0 =
+ * NULL meaning zeros.  h_in: DEVICE FP32 [count].  Step 3 is
+ * mamba_selective_scan with initial_state = h_in. */
+int mamba_scan_compose_prefix(const float *PH, int world, int rank, int64_t count,
+                              const float *h0, float *h_in, void *stream);
+
+/* Depthwise causal conv (causal_conv1d.metal:21-45), width K, optional
+ * bias and SiLU.  x, y strides {batch, time, channel}; w [dim, K] FP32;
+ * bias [dim] FP32 or NULL.  x and y share `dtype`. */
+int mamba_causal_conv1d(const void *x, const int64_t *x_stride, const float *w,
+                        const float *bias, void *y, const int64_t *y_stride, int batch,
+                        int seqlen, int dim, int K, int silu, int dtype, void *stream);
+
+/* Incremental conv (causal_conv1d.metal:50-82): conv over conv_state
+ * (oldest..newest) and x_t, then shift-append x_t.  x_t/y_t rows of
+ * `x_row_stride`/`y_row_stride` elements per batch row, channel stride 1;
+ * conv_state FP32 [batch, dim, K-1] updated in place. */
+int mamba_causal_conv1d_step(const void *x_t, int64_t x_row_stride, const float *w,
+                             const float *bias, void *y_t, int64_t y_row_stride,
+                             float *conv_state, int batch, int dim, int K, int silu,
+                             int dtype, void *stream);
+
+/* Single-token SSM update (state_update.metal:15-57, softplus always
+ * applied as in selective_scan_cpu.cpp:20), with optional dt_bias and
+ * SiLU(z) gate.  x, delta, z, y: rows of the given row strides (channel
+ * stride 1); B, C: rows of bc_row_stride elements (state stride 1);
+ * state FP32 [batch, dim, dstate] in place.  x, z, y share x_dtype;
+ * delta has delta_dtype; B/C have bc_dtype. */
+int mamba_ssm_step(const void *x, int64_t x_row_stride, const void *delta,
+                   int64_t delta_row_stride, const float *dt_bias, const void *B,
+                   const void *C, int64_t bc_row_stride, const float *A, const float *D,
+                   const void *z, int64_t z_row_stride, void *y, int64_t y_row_stride,
+                   float *state, int batch, int dim, int dstate, int x_dtype,
+                   int delta_dtype, int bc_dtype, void *stream);
+
+/* RMSNorm (rmsnorm.metal:11-81): y = x * rsqrt(mean(x^2) + eps) * w.
+ * x [rows, cols] of in_dtype, y [rows, cols] of out_dtype, w FP32 [cols]
+ * or NULL. */
+int mamba_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols, float eps,
+                  int in_dtype, int out_dtype, void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MAMBA_B200_H */

@@ -1,0 +1,160 @@
+// conv.cu -- depthwise causal conv1d (full sequence and incremental).
+//
+// Full sequence (Sources/Kernels/causal_conv1d.metal:21-45, with the SiLU of
+// MambaRuntime.cpp:96 fused into the epilogue):
+//   y[b,t,d] = SiLU( sum_{k<K} w[d,k] * x[b, t-K+1+k, d] + bias[d] )
+// One thread owns one channel and a run of TC consecutive timesteps; the
+// K-1 previous inputs live in a register window, so each input element is
+// read once (plus a K-1 halo per run) and every warp access is a contiguous
+// row segment when channels are contiguous.  Memory-bound: per (t,d) it
+// reads one x and writes one y.
+//
+// Incremental (causal_conv1d.metal:50-82): conv over conv_state
+// (oldest..newest) and the current x, then shift-append x into the state.
+#include "common.cuh"
+
+namespace mb {
+
+namespace {
+
+constexpr int kConvCH = 128;  // channels per CTA
+constexpr int kConvTC = 64;   // timesteps per thread run
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvCH)
+    conv1d_kernel(const T *__restrict__ x, int64_t sx0, int64_t sx1, int64_t sx2,
+                  const float *__restrict__ w, const float *__restrict__ bias, T *__restrict__ y,
+                  int64_t sy0, int64_t sy1, int64_t sy2, int L, int D, int silu) {
+    const int d = blockIdx.x * kConvCH + threadIdx.x;
+    const int b = blockIdx.z;
+    const int t0 = blockIdx.y * kConvTC;
+    if (d >= D) return;
+    const int t1 = min(L, t0 + kConvTC);
+    float wk[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) wk[k] = w[(int64_t)d * K + k];
+    const float bv = bias ? bias[d] : 0.f;
+    const T *xb = x + (int64_t)b * sx0 + (int64_t)d * sx2;
+    T *yb = y + (int64_t)b * sy0 + (int64_t)d * sy2;
+    float win[K];  // win[k] = x[t - K + 1 + k]
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int src = t0 - K + 1 + k;
+        win[k] = src >= 0 ? ld_f32(xb + (int64_t)src * sx1) : 0.f;
+    }
+    for (int t = t0; t < t1; ++t) {
+        win[K - 1] = ld_f32(xb + (int64_t)t * sx1);
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(win[k], wk[k], acc);
+        acc += bv;
+        if (silu) acc = silu_f(acc);
+        yb[(int64_t)t * sy1] = cvt_out<T>(acc);
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+    }
+}
+
+template <typename T, int K>
+__global__ void conv1d_step_kernel(const T *__restrict__ x, int64_t xrs, const float *__restrict__ w,
+                                   const float *__restrict__ bias, T *__restrict__ y, int64_t yrs,
+                                   float *__restrict__ state, int D, int silu) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    const int b = blockIdx.y;
+    if (d >= D) return;
+    float *st = state + ((int64_t)b * D + d) * (K - 1);
+    float win[K];
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) win[k] = st[k];
+    win[K - 1] = ld_f32(x + (int64_t)b * xrs + d);
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(win[k], w[(int64_t)d * K + k], acc);
+    if (bias) acc += bias[d];
+    if (silu) acc = silu_f(acc);
+    y[(int64_t)b * yrs + d] = cvt_out<T>(acc);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) st[k] = win[k + 1];
+}
+
+template <typename T, int K>
+int launch_conv_k(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
+                  const int64_t *sy, int batch, int L, int D, int silu, cudaStream_t st) {
+    dim3 grid(ceil_div(D, kConvCH), ceil_div(L, kConvTC), batch);
+    conv1d_kernel<T, K><<<grid, kConvCH, 0, st>>>(static_cast<const T *>(x), sx[0], sx[1], sx[2], w,
+                                                   bias, static_cast<T *>(y), sy[0], sy[1], sy[2],
+                                                   L, D, silu);
+    return launch_status("causal_conv1d kernel");
+}
+
+template <typename T>
+int launch_conv_t(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
+                  const int64_t *sy, int batch, int L, int D, int K, int silu, cudaStream_t st) {
+    switch (K) {
+        case 1: return launch_conv_k<T, 1>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 2: return launch_conv_k<T, 2>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 3: return launch_conv_k<T, 3>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 4: return launch_conv_k<T, 4>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 5: return launch_conv_k<T, 5>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 6: return launch_conv_k<T, 6>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 7: return launch_conv_k<T, 7>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+        case 8: return launch_conv_k<T, 8>(x, sx, w, bias, y, sy, batch, L, D, silu, st);
+    }
+    set_error("causal_conv1d: K must be in 1..8");
+    return -1;
+}
+
+template <typename T, int K>
+int launch_step_k(const void *x, int64_t xrs, const float *w, const float *bias, void *y, int64_t yrs,
+                  float *state, int batch, int D, int silu, cudaStream_t st) {
+    dim3 grid(ceil_div(D, 128), batch);
+    conv1d_step_kernel<T, K><<<grid, 128, 0, st>>>(static_cast<const T *>(x), xrs, w, bias,
+                                                    static_cast<T *>(y), yrs, state, D, silu);
+    return launch_status("causal_conv1d_step kernel");
+}
+
+template <typename T>
+int launch_step_t(const void *x, int64_t xrs, const float *w, const float *bias, void *y, int64_t yrs,
+                  float *state, int batch, int D, int K, int silu, cudaStream_t st) {
+    switch (K) {
+        case 1: return launch_step_k<T, 1>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 2: return launch_step_k<T, 2>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 3: return launch_step_k<T, 3>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 4: return launch_step_k<T, 4>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 5: return launch_step_k<T, 5>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 6: return launch_step_k<T, 6>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 7: return launch_step_k<T, 7>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+        case 8: return launch_step_k<T, 8>(x, xrs, w, bias, y, yrs, state, batch, D, silu, st);
+    }
+    set_error("causal_conv1d_step: K must be in 1..8");
+    return -1;
+}
+
+}  // namespace
+
+int causal_conv1d(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
+                  const int64_t *sy, int batch, int L, int D, int K, int silu, int dtype,
+                  cudaStream_t st) {
+    MB_CHECK_ARG(batch >= 0 && L >= 0 && D >= 0, "causal_conv1d: negative size");
+    MB_CHECK_ARG(batch <= 65535 && ceil_div(L, kConvTC) <= 65535, "causal_conv1d: grid too large");
+    if (batch == 0 || L == 0 || D == 0) return 0;
+    MB_CHECK_ARG(x && w && y && sx && sy, "causal_conv1d: null pointer");
+    if (dtype == MAMBA_F32) return launch_conv_t<float>(x, sx, w, bias, y, sy, batch, L, D, K, silu, st);
+    if (dtype == MAMBA_F16) return launch_conv_t<__half>(x, sx, w, bias, y, sy, batch, L, D, K, silu, st);
+    set_error("causal_conv1d: bad dtype");
+    return -1;
+}
+
+int causal_conv1d_step(const void *x, int64_t xrs, const float *w, const float *bias, void *y,
+                       int64_t yrs, float *state, int batch, int D, int K, int silu, int dtype,
+                       cudaStream_t st) {
+    MB_CHECK_ARG(batch >= 0 && D >= 0, "causal_conv1d_step: negative size");
+    if (batch == 0 || D == 0) return 0;
+    MB_CHECK_ARG(x && w && y && state, "causal_conv1d_step: null pointer");
+    if (dtype == MAMBA_F32) return launch_step_t<float>(x, xrs, w, bias, y, yrs, state, batch, D, K, silu, st);
+    if (dtype == MAMBA_F16) return launch_step_t<__half>(x, xrs, w, bias, y, yrs, state, batch, D, K, silu, st);
+    set_error("causal_conv1d_step: bad dtype");
+    return -1;
+}
+
+}  // namespace mb

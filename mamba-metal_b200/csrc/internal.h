@@ -1,0 +1,46 @@
+// internal.h -- declarations shared between the .cu translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "mamba.h"
+
+namespace mb {
+
+// scan.cu
+size_t scan_workspace_bytes(const MambaScanArgs *a);
+int selective_scan(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream_t st);
+int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws_bytes,
+                 cudaStream_t st);
+int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
+                        float *h_in, cudaStream_t st);
+
+// conv.cu
+int causal_conv1d(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
+                  const int64_t *sy, int batch, int L, int D, int K, int silu, int dtype,
+                  cudaStream_t st);
+int causal_conv1d_step(const void *x, int64_t xrs, const float *w, const float *bias, void *y,
+                       int64_t yrs, float *state, int batch, int D, int K, int silu, int dtype,
+                       cudaStream_t st);
+
+// norm.cu
+int rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols, float eps, int in_dt,
+            int out_dt, cudaStream_t st);
+
+// ssm_step.cu
+int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
+             const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
+             const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
+             int xd, int dd, int bd, cudaStream_t st);
+
+// init.cu
+uint64_t fill_key(uint64_t seed, int layer, int tag);
+int fill_random(void *out, int dtype, int64_t n, uint64_t key, int dist, float p0, float p1,
+                cudaStream_t st);
+int fill_A(float *A, int D, int N, cudaStream_t st);
+int fill_const(float *p, int64_t n, float v, cudaStream_t st);
+int transpose_cast(const float *src, void *dst, int dtype, int K, int N, cudaStream_t st);
+
+}  // namespace mb

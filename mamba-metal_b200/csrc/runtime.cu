@@ -1,0 +1,946 @@
+// runtime.cu -- the model runtime behind the C API.
+//
+// Replaces mamba::MambaRuntime (Sources/Mamba/MambaRuntime.hpp:27-64,
+// MambaRuntime.cpp:18-119) and its Metal device/buffer/pipeline layer
+// (Sources/Runtime/*) with a thin CUDA layer: one device, one stream and one
+// cuBLAS handle per model; weights resident in HBM in one allocation; an
+// activation arena sized for the largest batch*seq_len seen.
+//
+// Layer graph (the sequence written at MambaRuntime.cpp:93-101), tokens
+// row-major [T = batch*seq_len, features]:
+//   normed = RMSNorm(h)                            [T, d_model]   act
+//   xz     = normed @ in_proj                      [T, 2*d_inner] act
+//   u      = SiLU(causal_conv1d(xz[:, :d_inner]))  [T, d_inner]   act
+//   xdbc   = u @ x_proj                            [T, R + 2N]    act
+//   draw   = xdbc[:, :R] @ dt_proj                 [T, d_inner]   act
+//   y      = scan(u, draw + dt_bias, B, C, z = xz[:, d_inner:])  act
+//   h     += y @ out_proj                          [T, d_model]   FP32
+// The residual stream h stays FP32; activations use cfg.dtype.
+#include <cublas_v2.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace mb {
+
+// ---- errors ---------------------------------------------------------------
+namespace {
+thread_local std::string g_last_error;
+}
+void set_error(const std::string &msg) { g_last_error = msg; }
+const char *last_error() { return g_last_error.c_str(); }
+void clear_error() { g_last_error.clear(); }
+
+int device_sm_count() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+namespace {
+
+constexpr float kNormEps = 1e-5f;
+constexpr size_t kAlign = 256;
+constexpr size_t kCublasWs = 32u << 20;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Sets a device for the scope and restores the caller's device after.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// Move-only device allocation (replaces MetalBuffer, Sources/Runtime/MetalBuffer.hpp:7-28;
+// no unified memory: the host reaches it through explicit copies).
+struct DeviceBuffer {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer &) = delete;
+    DeviceBuffer &operator=(const DeviceBuffer &) = delete;
+    ~DeviceBuffer() { release(); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    int reserve(size_t n) {
+        if (n <= bytes) return 0;
+        release();
+        if (cudaMalloc(&ptr, n) != cudaSuccess) {
+            cudaGetLastError();
+            ptr = nullptr;
+            set_error("cudaMalloc of " + std::to_string(n) + " bytes failed");
+            return -1;
+        }
+        bytes = n;
+        return 0;
+    }
+};
+
+struct LayerWeights {
+    void *w_in_t = nullptr;   // [2D, M]    act  (in_proj^T)
+    void *w_x_t = nullptr;    // [R+2N, D]  act  (x_proj^T)
+    void *w_dt_t = nullptr;   // [D, R]     act  (dt_proj^T)
+    void *w_out_t = nullptr;  // [M, D]     act  (out_proj^T)
+    float *conv_w = nullptr;  // [D, K]
+    float *conv_b = nullptr;  // [D]
+    float *A = nullptr;       // [D, N]
+    float *Dskip = nullptr;   // [D]
+    float *norm_w = nullptr;  // [M]
+    float *dt_bias = nullptr; // [D]
+};
+
+// Per-operation CUDA-event timing (mamba_profile_*).  Events come from a
+// pool that is reused after every mamba_profile_enable.
+struct Profiler {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    struct Rec {
+        int op;
+        cudaEvent_t a, b;
+        int kernels;
+    };
+    std::vector<Rec> recs;
+    ~Profiler() {
+        for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    }
+    cudaEvent_t take() {
+        if (used == pool.size()) {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            pool.push_back(e);
+        }
+        return pool[used++];
+    }
+    void reset() {
+        used = 0;
+        recs.clear();
+    }
+};
+
+// Brackets one operation with an event pair while profiling is on.
+struct OpScope {
+    Profiler &p;
+    int op;
+    cudaStream_t st;
+    int kernels;
+    cudaEvent_t a = nullptr;
+    OpScope(Profiler &p_, int op_, cudaStream_t s, int k) : p(p_), op(op_), st(s), kernels(k) {
+        if (p.on && (a = p.take())) cudaEventRecord(a, st);
+    }
+    ~OpScope() {
+        if (!p.on || !a) return;
+        cudaEvent_t b = p.take();
+        if (b && cudaEventRecord(b, st) == cudaSuccess) p.recs.push_back({op, a, b, kernels});
+    }
+};
+
+}  // namespace
+
+struct Model {
+    MambaConfig cfg{};
+    int M = 0, D = 0, N = 0, K = 0, R = 0, XD = 0;
+    int act = MAMBA_F16;
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    cublasHandle_t cublas = nullptr;
+    DeviceBuffer cublas_ws;
+    DeviceBuffer weights;
+    std::vector<LayerWeights> layers;
+    // forward arena
+    DeviceBuffer arena;
+    int64_t arena_tokens = 0;
+    DeviceBuffer io;  // host-API staging for forward/step
+    // step arena
+    DeviceBuffer step_arena;
+    int64_t step_rows = 0;
+    // caller-provided stream (mamba_set_stream) and tracing
+    cudaStream_t user_stream = nullptr;
+    Profiler prof;
+
+    cudaStream_t cur_stream() const { return user_stream ? user_stream : stream; }
+
+    ~Model() {
+        if (stream) cudaStreamSynchronize(stream);
+        if (cublas) cublasDestroy(cublas);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    size_t act_size() const { return dtype_size(act); }
+
+    size_t layer_bytes() const {
+        const size_t a = act_size();
+        size_t s = 0;
+        s += align_up((size_t)2 * D * M * a);
+        s += align_up((size_t)XD * D * a);
+        s += align_up((size_t)D * R * a);
+        s += align_up((size_t)M * D * a);
+        s += align_up((size_t)D * K * 4);
+        s += align_up((size_t)D * 4);
+        s += align_up((size_t)D * N * 4);
+        s += align_up((size_t)D * 4);
+        s += align_up((size_t)M * 4);
+        s += align_up((size_t)D * 4);
+        return s;
+    }
+
+    int init(const MambaConfig &c) {
+        cfg = c;
+        M = c.d_model;
+        D = c.expand * c.d_model;
+        N = c.d_state;
+        K = c.d_conv;
+        R = (c.d_model + 15) / 16;
+        XD = R + 2 * N;
+        act = c.dtype;
+        MB_CUDA_TRY(cudaGetDevice(&dev));
+        cudaDeviceProp prop;
+        MB_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+        MB_CHECK_ARG(prop.major == 10, std::string("mamba_create: device '") + prop.name +
+                                           "' is not sm_100 (compute capability 10.x required)");
+        MB_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
+            set_error("cublasCreate failed");
+            return -1;
+        }
+        if (cublas_ws.reserve(kCublasWs)) return -1;
+        if (cublasSetWorkspace(cublas, cublas_ws.ptr, kCublasWs) != CUBLAS_STATUS_SUCCESS) {
+            set_error("cublasSetWorkspace failed");
+            return -1;
+        }
+        const size_t lb = layer_bytes();
+        if (weights.reserve(lb * c.n_layer)) return -1;
+        MB_CUDA_TRY(cudaMemsetAsync(weights.ptr, 0, lb * c.n_layer, stream));
+        layers.resize(c.n_layer);
+        const size_t a = act_size();
+        for (int l = 0; l < c.n_layer; ++l) {
+            char *p = static_cast<char *>(weights.ptr) + lb * l;
+            auto take = [&](size_t bytes) {
+                char *q = p;
+                p += align_up(bytes);
+                return q;
+            };
+            LayerWeights &w = layers[l];
+            w.w_in_t = take((size_t)2 * D * M * a);
+            w.w_x_t = take((size_t)XD * D * a);
+            w.w_dt_t = take((size_t)D * R * a);
+            w.w_out_t = take((size_t)M * D * a);
+            w.conv_w = reinterpret_cast<float *>(take((size_t)D * K * 4));
+            w.conv_b = reinterpret_cast<float *>(take((size_t)D * 4));
+            w.A = reinterpret_cast<float *>(take((size_t)D * N * 4));
+            w.Dskip = reinterpret_cast<float *>(take((size_t)D * 4));
+            w.norm_w = reinterpret_cast<float *>(take((size_t)M * 4));
+            w.dt_bias = reinterpret_cast<float *>(take((size_t)D * 4));
+        }
+        MB_CUDA_TRY(cudaStreamSynchronize(stream));
+        return 0;
+    }
+
+    // C[rows, n] (ldc) = A[rows, k] (lda) @ W where W is stored as Wt [n, k];
+    // beta = 1 accumulates into C (used for the residual).  C may be FP32
+    // while A/W are FP16 (FP32 accumulation in every case).
+    int gemm(cudaStream_t st, int64_t rows, int n, int k, const void *A, int lda, const void *Wt,
+             void *C, int ldc, int c_dtype, float beta) {
+        if (rows == 0 || n == 0) return 0;
+        MB_CHECK_ARG(rows <= 0x7fffffffLL, "gemm: too many rows");
+        const cudaDataType at = act == MAMBA_F16 ? CUDA_R_16F : CUDA_R_32F;
+        const cudaDataType ct = c_dtype == MAMBA_F16 ? CUDA_R_16F : CUDA_R_32F;
+        const float alpha = 1.f;
+        if (cublasSetStream(cublas, st) != CUBLAS_STATUS_SUCCESS) {
+            set_error("cublasSetStream failed");
+            return -1;
+        }
+        const cublasStatus_t s =
+            cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, n, (int)rows, k, &alpha, Wt, at, k, A, at,
+                         lda, &beta, C, ct, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (s != CUBLAS_STATUS_SUCCESS) {
+            set_error("cublasGemmEx failed with status " + std::to_string((int)s));
+            return -1;
+        }
+        return 0;
+    }
+
+    struct Arena {
+        void *normed, *xz, *u, *xdbc, *draw, *y, *scan_ws;
+        size_t scan_ws_bytes;
+    };
+
+    MambaScanArgs scan_args(const LayerWeights &w, const Arena &ar, int batch, int L) const {
+        MambaScanArgs s{};
+        const size_t a = act_size();
+        s.x = ar.u;
+        s.delta = ar.draw;
+        s.B = static_cast<const char *>(ar.xdbc) + (size_t)R * a;
+        s.C = static_cast<const char *>(ar.xdbc) + (size_t)(R + N) * a;
+        s.A = w.A;
+        s.D = w.Dskip;
+        s.y = ar.y;
+        s.final_state = nullptr;
+        s.z = static_cast<const char *>(ar.xz) + (size_t)D * a;
+        s.dt_bias = w.dt_bias;
+        s.initial_state = nullptr;
+        s.batch = batch;
+        s.seqlen = L;
+        s.dim = D;
+        s.dstate = N;
+        s.x_dtype = act;
+        s.delta_dtype = act;
+        s.bc_dtype = act;
+        s.chunk_len = 0;
+        const int64_t Ld = L;
+        const int64_t xs[3] = {Ld * D, D, 1};
+        const int64_t bcs[3] = {Ld * XD, XD, 1};
+        const int64_t zs[3] = {Ld * 2 * D, 2 * D, 1};
+        for (int i = 0; i < 3; ++i) {
+            s.x_stride[i] = xs[i];
+            s.delta_stride[i] = xs[i];
+            s.y_stride[i] = xs[i];
+            s.B_stride[i] = bcs[i];
+            s.C_stride[i] = bcs[i];
+            s.z_stride[i] = zs[i];
+        }
+        return s;
+    }
+
+    int ensure_arena(int batch, int L, Arena &ar) {
+        const int64_t T = (int64_t)batch * L;
+        const size_t a = act_size();
+        Arena probe{};
+        MambaScanArgs sa = scan_args(layers.empty() ? LayerWeights{} : layers[0], probe, batch, L);
+        const size_t ws = scan_workspace_bytes(&sa);
+        size_t need = align_up(T * M * a) + align_up(T * 2 * D * a) + align_up(T * D * a) +
+                      align_up(T * XD * a) + align_up(T * D * a) + align_up(T * D * a) + align_up(ws);
+        if (need > arena.bytes) {
+            // Work queued on either stream may still read the old arena.
+            MB_CUDA_TRY(cudaStreamSynchronize(stream));
+            MB_CUDA_TRY(cudaStreamSynchronize(cur_stream()));
+            if (arena.reserve(need)) return -1;
+        }
+        char *p = static_cast<char *>(arena.ptr);
+        auto take = [&](size_t bytes) {
+            char *q = p;
+            p += align_up(bytes);
+            return (void *)q;
+        };
+        ar.normed = take(T * M * a);
+        ar.xz = take(T * 2 * D * a);
+        ar.u = take(T * D * a);
+        ar.xdbc = take(T * XD * a);
+        ar.draw = take(T * D * a);
+        ar.y = take(T * D * a);
+        ar.scan_ws = ws ? take(ws) : nullptr;
+        ar.scan_ws_bytes = ws;
+        return 0;
+    }
+
+    int forward_device(const float *in, float *out, int batch, int L, cudaStream_t st) {
+        MB_CHECK_ARG(batch >= 0 && L >= 0, "forward: negative batch or seq_len");
+        const int64_t T = (int64_t)batch * L;
+        if (T == 0) return 0;
+        MB_CHECK_ARG(in && out, "forward: null pointer");
+        if (!st) st = cur_stream();
+        if (in != out) MB_CUDA_TRY(cudaMemcpyAsync(out, in, sizeof(float) * T * M, cudaMemcpyDeviceToDevice, st));
+        Arena ar{};
+        if (ensure_arena(batch, L, ar)) return -1;
+        const int64_t Ld = L;
+        const int64_t xs[3] = {Ld * 2 * D, 2 * D, 1};
+        const int64_t us[3] = {Ld * D, D, 1};
+        for (const LayerWeights &w : layers) {
+            {
+                OpScope o(prof, MAMBA_OP_RMSNORM, st, 1);
+                if (rmsnorm(out, w.norm_w, ar.normed, T, M, kNormEps, MAMBA_F32, act, st)) return -1;
+            }
+            {
+                OpScope o(prof, MAMBA_OP_IN_PROJ, st, 0);
+                if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f)) return -1;
+            }
+            {
+                OpScope o(prof, MAMBA_OP_CONV, st, 1);
+                if (causal_conv1d(ar.xz, xs, w.conv_w, w.conv_b, ar.u, us, batch, L, D, K, 1, act, st)) return -1;
+            }
+            {
+                OpScope o(prof, MAMBA_OP_X_PROJ, st, 0);
+                if (gemm(st, T, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, act, 0.f)) return -1;
+            }
+            {
+                OpScope o(prof, MAMBA_OP_DT_PROJ, st, 0);
+                if (gemm(st, T, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, act, 0.f)) return -1;
+            }
+            {
+                MambaScanArgs sa = scan_args(w, ar, batch, L);
+                OpScope o(prof, MAMBA_OP_SCAN, st, ar.scan_ws_bytes ? 3 : 1);
+                if (selective_scan(&sa, ar.scan_ws, ar.scan_ws_bytes, st)) return -1;
+            }
+            {
+                OpScope o(prof, MAMBA_OP_OUT_PROJ, st, 0);
+                if (gemm(st, T, M, D, ar.y, D, w.w_out_t, out, M, MAMBA_F32, 1.f)) return -1;
+            }
+        }
+        return 0;
+    }
+
+    int forward_host(const float *in, float *out, int batch, int L) {
+        MB_CHECK_ARG(batch >= 0 && L >= 0, "forward: negative batch or seq_len");
+        const int64_t T = (int64_t)batch * L;
+        if (T == 0) return 0;
+        MB_CHECK_ARG(in && out, "forward: null pointer");
+        const size_t bytes = sizeof(float) * T * M;
+        cudaStream_t st = cur_stream();
+        MB_CUDA_TRY(cudaStreamSynchronize(st));
+        if (io.reserve(bytes)) return -1;
+        float *d = static_cast<float *>(io.ptr);
+        MB_CUDA_TRY(cudaMemcpyAsync(d, in, bytes, cudaMemcpyHostToDevice, st));
+        if (forward_device(d, d, batch, L, st)) return -1;
+        MB_CUDA_TRY(cudaMemcpyAsync(out, d, bytes, cudaMemcpyDeviceToHost, st));
+        MB_CUDA_TRY(cudaStreamSynchronize(st));
+        return 0;
+    }
+};
+
+}  // namespace mb
+
+// ---- state handle -----------------------------------------------------------
+struct MambaStateHandle {
+    int dev = 0;
+    int batch = 0, n_layer = 0, D = 0, N = 0, K = 0;
+    float *conv = nullptr;  // [n_layer, batch, D, K-1]
+    float *ssm = nullptr;   // [n_layer, batch, D, N]
+    size_t conv_elems() const { return (size_t)n_layer * batch * D * (K - 1); }
+    size_t ssm_elems() const { return (size_t)n_layer * batch * D * N; }
+    ~MambaStateHandle() {
+        mb::DeviceGuard g(dev);
+        if (conv) cudaFree(conv);
+        if (ssm) cudaFree(ssm);
+    }
+};
+
+struct MambaModel {
+    std::unique_ptr<mb::Model> rt;
+};
+
+namespace mb {
+
+struct StepArena {
+    void *normed, *xz, *u, *xdbc, *draw, *y;
+};
+
+static int ensure_step_arena(Model &m, int rows, StepArena &ar) {
+    const size_t a = m.act_size();
+    const int64_t T = rows;
+    const size_t need = align_up(T * m.M * a) + align_up(T * 2 * m.D * a) + align_up(T * m.D * a) +
+                        align_up(T * m.XD * a) + align_up(T * m.D * a) + align_up(T * m.D * a);
+    if (need > m.step_arena.bytes) {
+        MB_CUDA_TRY(cudaStreamSynchronize(m.stream));
+        MB_CUDA_TRY(cudaStreamSynchronize(m.cur_stream()));
+        if (m.step_arena.reserve(need)) return -1;
+    }
+    char *p = static_cast<char *>(m.step_arena.ptr);
+    auto take = [&](size_t bytes) {
+        char *q = p;
+        p += align_up(bytes);
+        return (void *)q;
+    };
+    ar.normed = take(T * m.M * a);
+    ar.xz = take(T * 2 * m.D * a);
+    ar.u = take(T * m.D * a);
+    ar.xdbc = take(T * m.XD * a);
+    ar.draw = take(T * m.D * a);
+    ar.y = take(T * m.D * a);
+    return 0;
+}
+
+static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *out, cudaStream_t st) {
+    MB_CHECK_ARG(tok && out, "step: null pointer");
+    MB_CHECK_ARG(s.dev == m.dev && s.n_layer == m.cfg.n_layer && s.D == m.D && s.N == m.N && s.K == m.K,
+                 "step: state does not belong to this model's configuration");
+    const int Bt = s.batch;
+    if (Bt == 0) return 0;
+    if (!st) st = m.cur_stream();
+    if (tok != out)
+        MB_CUDA_TRY(cudaMemcpyAsync(out, tok, sizeof(float) * Bt * m.M, cudaMemcpyDeviceToDevice, st));
+    StepArena ar{};
+    if (ensure_step_arena(m, Bt, ar)) return -1;
+    const size_t a = m.act_size();
+    const int D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
+    Profiler &pf = m.prof;
+    for (int l = 0; l < m.cfg.n_layer; ++l) {
+        const LayerWeights &w = m.layers[l];
+        float *conv_state = s.conv + (size_t)l * Bt * D * (K - 1);
+        float *ssm_state = s.ssm + (size_t)l * Bt * D * N;
+        {
+            OpScope o(pf, MAMBA_OP_RMSNORM, st, 1);
+            if (rmsnorm(out, w.norm_w, ar.normed, Bt, m.M, kNormEps, MAMBA_F32, m.act, st)) return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_IN_PROJ, st, 0);
+            if (m.gemm(st, Bt, 2 * D, m.M, ar.normed, m.M, w.w_in_t, ar.xz, 2 * D, m.act, 0.f)) return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_CONV, st, 1);
+            if (causal_conv1d_step(ar.xz, 2 * D, w.conv_w, w.conv_b, ar.u, D, conv_state, Bt, D, K, 1, m.act,
+                                   st))
+                return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_X_PROJ, st, 0);
+            if (m.gemm(st, Bt, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, m.act, 0.f)) return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_DT_PROJ, st, 0);
+            if (m.gemm(st, Bt, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, m.act, 0.f)) return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_SCAN, st, 1);
+            const char *xdbc = static_cast<const char *>(ar.xdbc);
+            if (ssm_step(ar.u, D, ar.draw, D, w.dt_bias, xdbc + (size_t)R * a, xdbc + (size_t)(R + N) * a, XD,
+                         w.A, w.Dskip, static_cast<const char *>(ar.xz) + (size_t)D * a, 2 * D, ar.y, D,
+                         ssm_state, Bt, D, N, m.act, m.act, m.act, st))
+                return -1;
+        }
+        {
+            OpScope o(pf, MAMBA_OP_OUT_PROJ, st, 0);
+            if (m.gemm(st, Bt, m.M, D, ar.y, D, w.w_out_t, out, m.M, MAMBA_F32, 1.f)) return -1;
+        }
+    }
+    return 0;
+}
+
+// ---- weights -----------------------------------------------------------------
+namespace {
+
+constexpr char kBlobMagic[8] = {'M', 'A', 'M', 'B', 'A', 'B', '2', 0};
+constexpr uint32_t kBlobVersion = 1;
+constexpr uint32_t kBlobHeader = 64;
+
+bool config_valid(const MambaConfig *c, std::string &why) {
+    if (!c) {
+        why = "null config";
+        return false;
+    }
+    if (c->d_model <= 0 || c->expand <= 0 || c->n_layer <= 0) {
+        why = "d_model, expand and n_layer must be positive";
+        return false;
+    }
+    if (c->d_state < 1 || c->d_state > 16) {
+        why = "d_state must be in 1..16";
+        return false;
+    }
+    if (c->d_conv < 1 || c->d_conv > 8) {
+        why = "d_conv must be in 1..8";
+        return false;
+    }
+    if (c->dtype != MAMBA_F32 && c->dtype != MAMBA_F16) {
+        why = "dtype must be MAMBA_F32 or MAMBA_F16";
+        return false;
+    }
+    if ((int64_t)c->expand * c->d_model > (1 << 24)) {
+        why = "d_inner too large";
+        return false;
+    }
+    return true;
+}
+
+size_t layer_floats(const MambaConfig &c) {
+    const size_t M = c.d_model, D = (size_t)c.expand * c.d_model, N = c.d_state, K = c.d_conv;
+    const size_t R = (M + 15) / 16;
+    return M * 2 * D + D * K + D + D * (R + 2 * N) + R * D + D * N + D + D * M + M + D;
+}
+
+}  // namespace
+
+static int load_weights(Model &m, const void *data, size_t size) {
+    MB_CHECK_ARG(data != nullptr, "load_weights: null blob");
+    MB_CHECK_ARG(size >= kBlobHeader, "load_weights: blob shorter than its 64-byte header");
+    const char *p = static_cast<const char *>(data);
+    MB_CHECK_ARG(std::memcmp(p, kBlobMagic, 8) == 0, "load_weights: bad magic (expected MAMBAB2)");
+    uint32_t ver, hdr;
+    std::memcpy(&ver, p + 8, 4);
+    std::memcpy(&hdr, p + 12, 4);
+    MB_CHECK_ARG(ver == kBlobVersion && hdr == kBlobHeader, "load_weights: unsupported blob version");
+    MambaConfig bc;
+    std::memcpy(&bc, p + 16, sizeof(bc));
+    MB_CHECK_ARG(std::memcmp(&bc, &m.cfg, sizeof(bc)) == 0, "load_weights: blob config differs from the model's");
+    int32_t r;
+    std::memcpy(&r, p + 40, 4);
+    MB_CHECK_ARG(r == m.R, "load_weights: blob dt_rank differs");
+    const size_t per = layer_floats(m.cfg);
+    MB_CHECK_ARG(size == kBlobHeader + per * 4 * (size_t)m.cfg.n_layer, "load_weights: blob size mismatch");
+    DeviceBuffer stage;
+    if (stage.reserve(per * 4)) return -1;
+    const int M = m.M, D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
+    cudaStream_t st = m.stream;
+    for (int l = 0; l < m.cfg.n_layer; ++l) {
+        const float *src = reinterpret_cast<const float *>(p + kBlobHeader) + per * l;
+        MB_CUDA_TRY(cudaMemcpyAsync(stage.ptr, src, per * 4, cudaMemcpyHostToDevice, st));
+        const float *s = static_cast<const float *>(stage.ptr);
+        LayerWeights &w = m.layers[l];
+        if (transpose_cast(s, w.w_in_t, m.act, M, 2 * D, st)) return -1;
+        s += (size_t)M * 2 * D;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.conv_w, s, (size_t)D * K * 4, cudaMemcpyDeviceToDevice, st));
+        s += (size_t)D * K;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.conv_b, s, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        s += D;
+        if (transpose_cast(s, w.w_x_t, m.act, D, XD, st)) return -1;
+        s += (size_t)D * XD;
+        if (transpose_cast(s, w.w_dt_t, m.act, R, D, st)) return -1;
+        s += (size_t)R * D;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.A, s, (size_t)D * N * 4, cudaMemcpyDeviceToDevice, st));
+        s += (size_t)D * N;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.Dskip, s, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        s += D;
+        if (transpose_cast(s, w.w_out_t, m.act, D, M, st)) return -1;
+        s += (size_t)D * M;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.norm_w, s, (size_t)M * 4, cudaMemcpyDeviceToDevice, st));
+        s += M;
+        MB_CUDA_TRY(cudaMemcpyAsync(w.dt_bias, s, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        // The staging buffer is reused by the next layer.
+        MB_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return 0;
+}
+
+enum Tag { kTagIn = 1, kTagConvW, kTagConvB, kTagX, kTagDt, kTagOut, kTagDtBias };
+
+static int init_random(Model &m, uint64_t seed) {
+    cudaStream_t st = m.stream;
+    const int M = m.M, D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
+    for (int l = 0; l < m.cfg.n_layer; ++l) {
+        LayerWeights &w = m.layers[l];
+        if (fill_random(w.w_in_t, m.act, (int64_t)2 * D * M, fill_key(seed, l, kTagIn), 0, 0.f, 0.02f, st)) return -1;
+        if (fill_random(w.conv_w, MAMBA_F32, (int64_t)D * K, fill_key(seed, l, kTagConvW), 1, -0.5f, 0.5f, st)) return -1;
+        if (fill_random(w.conv_b, MAMBA_F32, D, fill_key(seed, l, kTagConvB), 1, -0.5f, 0.5f, st)) return -1;
+        if (fill_random(w.w_x_t, m.act, (int64_t)XD * D, fill_key(seed, l, kTagX), 0, 0.f, 0.02f, st)) return -1;
+        if (fill_random(w.w_dt_t, m.act, (int64_t)D * R, fill_key(seed, l, kTagDt), 0, 0.f, 0.02f, st)) return -1;
+        if (fill_random(w.w_out_t, m.act, (int64_t)M * D, fill_key(seed, l, kTagOut), 0, 0.f, 0.02f, st)) return -1;
+        if (fill_random(w.dt_bias, MAMBA_F32, D, fill_key(seed, l, kTagDtBias), 2, 1e-3f, 1e-1f, st)) return -1;
+        if (fill_A(w.A, D, N, st)) return -1;
+        if (fill_const(w.Dskip, D, 1.f, st)) return -1;
+        if (fill_const(w.norm_w, M, 1.f, st)) return -1;
+    }
+    MB_CUDA_TRY(cudaStreamSynchronize(st));
+    return 0;
+}
+
+}  // namespace mb
+
+// ============================================================================
+// C API
+// ============================================================================
+using mb::set_error;
+
+extern "C" {
+
+MambaModel *mamba_create(const MambaConfig *cfg) {
+    mb::clear_error();
+    std::string why;
+    if (!mb::config_valid(cfg, why)) {
+        set_error("mamba_create: " + why);
+        return nullptr;
+    }
+    auto *m = new MambaModel;
+    m->rt = std::make_unique<mb::Model>();
+    if (m->rt->init(*cfg)) {
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+
+void mamba_destroy(MambaModel *m) {
+    if (!m) return;
+    if (m->rt) {
+        mb::DeviceGuard g(m->rt->dev);
+        m->rt.reset();
+    }
+    delete m;
+}
+
+int mamba_load_weights(MambaModel *m, const void *data, size_t size) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_load_weights: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    return mb::load_weights(*m->rt, data, size) ? -1 : 0;
+}
+
+int mamba_forward(MambaModel *m, const float *input, float *output, int batch, int seq_len) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_forward: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    return m->rt->forward_host(input, output, batch, seq_len) ? -1 : 0;
+}
+
+MambaStateHandle *mamba_create_state(MambaModel *m, int batch) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_create_state: null model");
+        return nullptr;
+    }
+    if (batch < 0 || batch > 65535) {
+        set_error("mamba_create_state: batch must be in 0..65535");
+        return nullptr;
+    }
+    mb::Model &rt = *m->rt;
+    mb::DeviceGuard g(rt.dev);
+    auto *s = new MambaStateHandle;
+    s->dev = rt.dev;
+    s->batch = batch;
+    s->n_layer = rt.cfg.n_layer;
+    s->D = rt.D;
+    s->N = rt.N;
+    s->K = rt.K;
+    const size_t cb = std::max<size_t>(s->conv_elems(), 1) * 4, sb = std::max<size_t>(s->ssm_elems(), 1) * 4;
+    if (cudaMalloc(&s->conv, cb) != cudaSuccess || cudaMalloc(&s->ssm, sb) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("mamba_create_state: cudaMalloc failed");
+        delete s;
+        return nullptr;
+    }
+    if (cudaMemset(s->conv, 0, cb) != cudaSuccess || cudaMemset(s->ssm, 0, sb) != cudaSuccess) {
+        set_error("mamba_create_state: cudaMemset failed");
+        delete s;
+        return nullptr;
+    }
+    return s;
+}
+
+void mamba_reset_state(MambaStateHandle *s) {
+    if (!s) return;
+    mb::DeviceGuard g(s->dev);
+    if (s->conv) cudaMemset(s->conv, 0, std::max<size_t>(s->conv_elems(), 1) * 4);
+    if (s->ssm) cudaMemset(s->ssm, 0, std::max<size_t>(s->ssm_elems(), 1) * 4);
+}
+
+int mamba_step(MambaModel *m, MambaStateHandle *s, const float *token, float *out) {
+    mb::clear_error();
+    if (!m || !m->rt || !s) {
+        set_error("mamba_step: null model or state");
+        return -1;
+    }
+    mb::Model &rt = *m->rt;
+    mb::DeviceGuard g(rt.dev);
+    if (!token || !out) {
+        set_error("mamba_step: null pointer");
+        return -1;
+    }
+    const size_t bytes = sizeof(float) * (size_t)s->batch * rt.M;
+    if (bytes == 0) return 0;
+    cudaStream_t st_ = rt.cur_stream();
+    if (cudaStreamSynchronize(st_) != cudaSuccess || rt.io.reserve(bytes)) {
+        if (!*mb::last_error()) set_error("mamba_step: device error");
+        return -1;
+    }
+    float *d = static_cast<float *>(rt.io.ptr);
+    if (cudaMemcpyAsync(d, token, bytes, cudaMemcpyHostToDevice, st_) != cudaSuccess) {
+        set_error("mamba_step: host-to-device copy failed");
+        return -1;
+    }
+    if (mb::step_device(rt, *s, d, d, st_)) return -1;
+    if (cudaMemcpyAsync(out, d, bytes, cudaMemcpyDeviceToHost, st_) != cudaSuccess ||
+        cudaStreamSynchronize(st_) != cudaSuccess) {
+        set_error("mamba_step: device-to-host copy failed");
+        return -1;
+    }
+    return 0;
+}
+
+void mamba_destroy_state(MambaStateHandle *s) { delete s; }
+
+const char *mamba_last_error(void) { return mb::last_error(); }
+
+int mamba_dt_rank(const MambaConfig *cfg) { return cfg ? (cfg->d_model + 15) / 16 : -1; }
+
+size_t mamba_weights_blob_size(const MambaConfig *cfg) {
+    std::string why;
+    if (!mb::config_valid(cfg, why)) return 0;
+    return mb::kBlobHeader + mb::layer_floats(*cfg) * 4 * (size_t)cfg->n_layer;
+}
+
+int mamba_init_weights_random(MambaModel *m, uint64_t seed) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_init_weights_random: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    return mb::init_random(*m->rt, seed) ? -1 : 0;
+}
+
+int mamba_forward_device(MambaModel *m, const float *input, float *output, int batch, int seq_len,
+                         void *stream) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_forward_device: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    return m->rt->forward_device(input, output, batch, seq_len, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_step_device(MambaModel *m, MambaStateHandle *s, const float *token, float *out, void *stream) {
+    mb::clear_error();
+    if (!m || !m->rt || !s) {
+        set_error("mamba_step_device: null model or state");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    return mb::step_device(*m->rt, *s, token, out, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_state_batch(const MambaStateHandle *s) { return s ? s->batch : -1; }
+
+int mamba_state_buffers(MambaStateHandle *s, int layer, float **conv_state, float **ssm_state) {
+    if (!s || layer < 0 || layer >= s->n_layer) {
+        set_error("mamba_state_buffers: bad state or layer");
+        return -1;
+    }
+    if (conv_state) *conv_state = s->conv + (size_t)layer * s->batch * s->D * (s->K - 1);
+    if (ssm_state) *ssm_state = s->ssm + (size_t)layer * s->batch * s->D * s->N;
+    return 0;
+}
+
+int mamba_set_stream(MambaModel *m, void *stream) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_set_stream: null model");
+        return -1;
+    }
+    m->rt->user_stream = static_cast<cudaStream_t>(stream);
+    return 0;
+}
+
+int mamba_profile_enable(MambaModel *m, int on) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_profile_enable: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    if (cudaStreamSynchronize(m->rt->cur_stream()) != cudaSuccess) {
+        set_error("mamba_profile_enable: stream error");
+        return -1;
+    }
+    m->rt->prof.reset();
+    m->rt->prof.on = on != 0;
+    return 0;
+}
+
+int mamba_profile_read(MambaModel *m, int op, double *total_ms, int64_t *calls, int64_t *kernels) {
+    mb::clear_error();
+    if (!m || !m->rt || op < 0 || op >= MAMBA_OP_COUNT) {
+        set_error("mamba_profile_read: bad model or op");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    double tot = 0.0;
+    int64_t n = 0, k = 0;
+    for (const auto &r : m->rt->prof.recs) {
+        if (r.op != op) continue;
+        float ms = 0.f;
+        if (cudaEventSynchronize(r.b) != cudaSuccess || cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) {
+            set_error("mamba_profile_read: event query failed");
+            return -1;
+        }
+        tot += ms;
+        ++n;
+        k += r.kernels;
+    }
+    if (total_ms) *total_ms = tot;
+    if (calls) *calls = n;
+    if (kernels) *kernels = k;
+    return 0;
+}
+
+// ---- Part 3: kernels on device pointers --------------------------------------
+size_t mamba_selective_scan_workspace(const MambaScanArgs *a) { return mb::scan_workspace_bytes(a); }
+
+int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes, void *stream) {
+    mb::clear_error();
+    return mb::selective_scan(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_scan_summary(const MambaScanArgs *a, float *P, float *H, void *workspace, size_t workspace_bytes,
+                       void *stream) {
+    mb::clear_error();
+    return mb::scan_summary(a, P, H, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
+                              float *h_in, void *stream) {
+    mb::clear_error();
+    return mb::scan_compose_prefix(PH, world, rank, count, h0, h_in, static_cast<cudaStream_t>(stream)) ? -1
+                                                                                                         : 0;
+}
+
+int mamba_causal_conv1d(const void *x, const int64_t *x_stride, const float *w, const float *bias, void *y,
+                        const int64_t *y_stride, int batch, int seqlen, int dim, int K, int silu, int dtype,
+                        void *stream) {
+    mb::clear_error();
+    return mb::causal_conv1d(x, x_stride, w, bias, y, y_stride, batch, seqlen, dim, K, silu, dtype,
+                             static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
+}
+
+int mamba_causal_conv1d_step(const void *x_t, int64_t x_row_stride, const float *w, const float *bias,
+                             void *y_t, int64_t y_row_stride, float *conv_state, int batch, int dim, int K,
+                             int silu, int dtype, void *stream) {
+    mb::clear_error();
+    return mb::causal_conv1d_step(x_t, x_row_stride, w, bias, y_t, y_row_stride, conv_state, batch, dim, K,
+                                  silu, dtype, static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
+}
+
+int mamba_ssm_step(const void *x, int64_t x_row_stride, const void *delta, int64_t delta_row_stride,
+                   const float *dt_bias, const void *B, const void *C, int64_t bc_row_stride, const float *A,
+                   const float *D, const void *z, int64_t z_row_stride, void *y, int64_t y_row_stride,
+                   float *state, int batch, int dim, int dstate, int x_dtype, int delta_dtype, int bc_dtype,
+                   void *stream) {
+    mb::clear_error();
+    return mb::ssm_step(x, x_row_stride, delta, delta_row_stride, dt_bias, B, C, bc_row_stride, A, D, z,
+                        z_row_stride, y, y_row_stride, state, batch, dim, dstate, x_dtype, delta_dtype,
+                        bc_dtype, static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
+}
+
+int mamba_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols, float eps, int in_dtype,
+                  int out_dtype, void *stream) {
+    mb::clear_error();
+    return mb::rmsnorm(x, w, y, rows, cols, eps, in_dtype, out_dtype, static_cast<cudaStream_t>(stream)) ? -1
+                                                                                                        : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,149 @@
+// ssm_step.cu -- single-token SSM state update for decode
+// (Sources/Kernels/state_update.metal:15-57), with softplus always applied
+// as in the reference oracle (Sources/CPURef/selective_scan_cpu.cpp:20),
+// the dt bias added before it, and the SiLU(z) gate fused:
+//   dt = softplus(delta + dt_bias)
+//   h[n] = exp(dt*A[d,n]) * h[n] + (exp(dt*A)-1)/A * B[n] * x
+//   y = (sum_n C[n]*h[n] + D*x) * SiLU(z)
+// One thread per (b, d); its N FP32 states are a contiguous 64-byte run, so
+// a warp reads and writes 2 KB of state with 16-byte vector accesses.  The
+// arithmetic is the same sequence the full-sequence scan uses, so T decode
+// steps reproduce a T-token forward.  HBM-bound on the state read-modify-
+// write (8*N bytes per (b,d)).
+#include "common.cuh"
+
+namespace mb {
+
+namespace {
+
+__device__ __forceinline__ float ex2_approx(float v) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+template <int NS, typename Tx, typename Tdt, typename Tbc>
+__global__ void __launch_bounds__(128)
+    ssm_step_kernel(const Tx *__restrict__ x, int64_t xrs, const Tdt *__restrict__ delta, int64_t drs,
+                    const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
+                    const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
+                    const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
+                    Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N) {
+    __shared__ float sB[NS], sC[NS];
+    const int b = blockIdx.y;
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (threadIdx.x < NS) {
+        const int n = threadIdx.x;
+        sB[n] = n < N ? ld_f32(Bm + (int64_t)b * bcrs + n) : 0.f;
+        sC[n] = n < N ? ld_f32(Cm + (int64_t)b * bcrs + n) : 0.f;
+    }
+    __syncthreads();
+    if (d >= D) return;
+    const float xv = ld_f32(x + (int64_t)b * xrs + d);
+    float draw = ld_f32(delta + (int64_t)b * drs + d);
+    if (dt_bias) draw = draw + dt_bias[d];
+    const float dt = softplus_f(draw);
+    float *hp = state + ((int64_t)b * D + d) * N;
+    float h[NS];
+    const bool vec = (NS == N) && (NS % 4 == 0);
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < NS / 4; ++i) {
+            const float4 v = reinterpret_cast<const float4 *>(hp)[i];
+            h[4 * i] = v.x;
+            h[4 * i + 1] = v.y;
+            h[4 * i + 2] = v.z;
+            h[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int n = 0; n < NS; ++n) h[n] = n < N ? hp[n] : 0.f;
+    }
+    float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < NS; ++n) {
+        const float a_c = n < N ? A[(int64_t)d * N + n] : 0.f;
+        const float a = ex2_approx(dt * (a_c * kLog2e));
+        const float w = xv * sB[n];
+        float bb;
+        if (fabsf(a_c) > 1e-6f) {
+            const float k = w * (1.0f / a_c);
+            bb = fmaf(a, k, -k);
+        } else {
+            bb = dt * w;
+        }
+        h[n] = fmaf(a, h[n], bb);
+        if (n & 1) y1 = fmaf(sC[n], h[n], y1);
+        else y0 = fmaf(sC[n], h[n], y0);
+    }
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < NS / 4; ++i)
+            reinterpret_cast<float4 *>(hp)[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    } else {
+#pragma unroll
+        for (int n = 0; n < NS; ++n)
+            if (n < N) hp[n] = h[n];
+    }
+    const float dsk = Dskip ? Dskip[d] : 0.f;
+    float yv = fmaf(dsk, xv, y0 + y1);
+    if (z) yv *= silu_f(ld_f32(z + (int64_t)b * zrs + d));
+    y[(int64_t)b * yrs + d] = cvt_out<Tx>(yv);
+}
+
+template <int NS, typename Tx, typename Tdt, typename Tbc>
+int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
+                const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
+                const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
+                int N, cudaStream_t st) {
+    dim3 grid(ceil_div(D, 128), batch);
+    ssm_step_kernel<NS, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
+        static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
+        static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
+        static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, D, N);
+    return launch_status("ssm_step kernel");
+}
+
+template <typename Tx, typename Tdt, typename Tbc>
+int launch_step_ns(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
+                   const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
+                   const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
+                   int N, cudaStream_t st) {
+    if (N <= 4)
+        return launch_step<4, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
+                                            yrs, state, batch, D, N, st);
+    if (N <= 8)
+        return launch_step<8, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
+                                            yrs, state, batch, D, N, st);
+    return launch_step<16, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
+                                         yrs, state, batch, D, N, st);
+}
+
+}  // namespace
+
+int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
+             const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
+             const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
+             int xd, int dd, int bd, cudaStream_t st) {
+    MB_CHECK_ARG(batch >= 0 && D >= 0, "ssm_step: negative size");
+    MB_CHECK_ARG(N >= 1 && N <= 16, "ssm_step: dstate must be in 1..16");
+    MB_CHECK_ARG(batch <= 65535, "ssm_step: batch > 65535");
+    if (batch == 0 || D == 0) return 0;
+    MB_CHECK_ARG(x && delta && B && C && A && y && state, "ssm_step: null pointer");
+    if (xd == MAMBA_F32 && dd == MAMBA_F32 && bd == MAMBA_F32)
+        return launch_step_ns<float, float, float>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs,
+                                                   y, yrs, state, batch, D, N, st);
+    if (xd == MAMBA_F16 && dd == MAMBA_F16 && bd == MAMBA_F16)
+        return launch_step_ns<__half, __half, __half>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
+                                                      zrs, y, yrs, state, batch, D, N, st);
+    if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F16)
+        return launch_step_ns<__half, float, __half>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
+                                                     zrs, y, yrs, state, batch, D, N, st);
+    if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F32)
+        return launch_step_ns<__half, float, float>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
+                                                    zrs, y, yrs, state, batch, D, N, st);
+    set_error("ssm_step: unsupported dtype combination");
+    return -1;
+}
+
+}  // namespace mb

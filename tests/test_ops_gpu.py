@@ -1,0 +1,118 @@
+"""GPU parity of conv, conv step, SSM step and RMSNorm kernels (through the
+C ABI) against the oracle restatements."""
+import numpy as np
+import pytest
+import torch
+
+import mamba_b200 as mb
+import oracle
+from test_scan_gpu import TOL16, TOL32, dev, err, r16, scan_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_causal_conv1d(cuda, K, dtype):
+    """x read as the first half of an interleaved [b, L, 2D] buffer (the
+    in_proj output layout), SiLU fused."""
+    rng = np.random.default_rng(K)
+    bsz, L, D = 3, 150, 200
+    xz = rng.standard_normal((bsz, L, 2 * D)).astype(np.float32)
+    if dtype == torch.float16:
+        xz = r16(xz)
+    w = rng.uniform(-0.5, 0.5, (D, K)).astype(np.float32)
+    b = rng.uniform(-0.5, 0.5, D).astype(np.float32)
+    y_ref = oracle.causal_conv1d(xz[..., :D], w, b, silu=True)
+    txz = dev(xz, dtype)
+    y = mb.causal_conv1d(txz[..., :D], dev(w), dev(b), silu=True)
+    torch.cuda.synchronize()
+    assert err(y, y_ref) < (TOL32 if dtype == torch.float32 else TOL16)
+
+
+def test_causal_conv1d_time_contiguous_no_bias(cuda):
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((2, 77, 33)).astype(np.float32)
+    w = rng.uniform(-0.5, 0.5, (33, 4)).astype(np.float32)
+    y_ref = oracle.causal_conv1d(x, w, None, silu=False)
+    y = mb.causal_conv1d(dev(x, time_major=False), dev(w), None, silu=False)
+    torch.cuda.synchronize()
+    assert err(y, y_ref) < TOL32
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_conv_step_sequence(cuda, dtype):
+    rng = np.random.default_rng(12)
+    bsz, L, D, K = 4, 10, 96, 4
+    x = rng.standard_normal((bsz, L, D)).astype(np.float32)
+    if dtype == torch.float16:
+        x = r16(x)
+    w = rng.uniform(-0.5, 0.5, (D, K)).astype(np.float32)
+    b = rng.uniform(-0.5, 0.5, D).astype(np.float32)
+    st_ref = np.zeros((bsz, D, K - 1), np.float32)
+    st = torch.zeros((bsz, D, K - 1), device="cuda")
+    tx, tw, tb = dev(x, dtype), dev(w), dev(b)
+    for t in range(L):
+        yr = oracle.causal_conv1d_step(x[:, t], w, b, st_ref, silu=True)
+        y = mb.causal_conv1d_step(tx[:, t], tw, tb, st, silu=True)
+        torch.cuda.synchronize()
+        assert err(y, yr) < (TOL32 if dtype == torch.float32 else TOL16)
+    assert np.array_equal(st.cpu().numpy(), st_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_ssm_step_sequence(cuda, dtype):
+    """T decode updates equal the oracle step (and so the scan)."""
+    bsz, L, D, N = 5, 12, 160, 16
+    x, dr, B, C, z, A, Dk = scan_inputs(13, bsz, L, D, N)
+    bias = np.random.default_rng(0).normal(0, 0.5, D).astype(np.float32)
+    if dtype == torch.float16:
+        x, dr, B, C, z = map(r16, (x, dr, B, C, z))
+    st_ref = np.zeros((bsz, D, N), np.float32)
+    st = torch.zeros((bsz, D, N), device="cuda")
+    tA, tD, tb = dev(A), dev(Dk), dev(bias)
+    tx, tdr, tB, tC, tz = (dev(a, dtype) for a in (x, dr, B, C, z))
+    for t in range(L):
+        yr = oracle.ssm_step(x[:, t], dr[:, t], B[:, t], C[:, t], A, Dk, st_ref, z=z[:, t],
+                             dt_bias=bias)
+        y = mb.ssm_step(tx[:, t], tdr[:, t], tA, tB[:, t], tC[:, t], st, D=tD, z=tz[:, t],
+                        dt_bias=tb)
+        torch.cuda.synchronize()
+        assert err(y, yr) < (TOL32 if dtype == torch.float32 else TOL16)
+    assert err(st, st_ref) < TOL32
+
+
+def test_ssm_step_matches_scan_final_state(cuda):
+    bsz, L, D, N = 2, 40, 64, 8
+    x, dr, B, C, z, A, Dk = scan_inputs(14, bsz, L, D, N)
+    tx, tdr, tA, tB, tC, tz, tD = dev(x), dev(dr), dev(A), dev(B), dev(C), dev(z), dev(Dk)
+    y_scan, h_scan = mb.selective_scan(tx, tdr, tA, tB, tC, D=tD, z=tz, return_final_state=True)
+    st = torch.zeros((bsz, D, N), device="cuda")
+    ys = [mb.ssm_step(tx[:, t], tdr[:, t], tA, tB[:, t], tC[:, t], st, D=tD, z=tz[:, t])
+          for t in range(L)]
+    torch.cuda.synchronize()
+    # same arithmetic sequence in both kernels
+    assert torch.allclose(torch.stack(ys, 1), y_scan, rtol=1e-6, atol=1e-6)
+    assert torch.allclose(st, h_scan, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("cols", [768, 2048, 2560, 100, 4100])
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_rmsnorm(cuda, cols, out):
+    rng = np.random.default_rng(cols)
+    rows = 257
+    x = (rng.standard_normal((rows, cols)) * 3).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+    y_ref = oracle.rmsnorm(x, w, 1e-5)
+    y = mb.rmsnorm(dev(x), dev(w), 1e-5, out_dtype=out)
+    torch.cuda.synchronize()
+    assert err(y, y_ref) < (1e-6 if out == torch.float32 else 1e-3)
+
+
+def test_rmsnorm_fp16_input_no_weight(cuda):
+    rng = np.random.default_rng(3)
+    x = r16(rng.standard_normal((64, 512)).astype(np.float32))
+    y_ref = oracle.rmsnorm(x, None, 1e-5)
+    y = mb.rmsnorm(dev(x, torch.float16), None, 1e-5)
+    torch.cuda.synchronize()
+    assert err(y, y_ref) < 1e-3
