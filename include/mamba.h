@@ -97,6 +97,12 @@ void mamba_destroy_state(MambaStateHandle *s);
  * reference only prints to stderr (MambaRuntime.cpp:42,65). */
 const char *mamba_last_error(void);
 
+/* Error flags raised by kernels on the current device since the last
+ * clear (0 = none).  Bit 0: a shared-memory pipeline wait inside the
+ * selective scan exceeded its 2-second bound, so that call stopped early and
+ * its outputs are invalid.  Waits for the device; clear != 0 resets them. */
+unsigned mamba_device_status(int clear);
+
 /* dt_rank used for a config: ceil(d_model / 16). */
 int mamba_dt_rank(const MambaConfig *cfg);
 

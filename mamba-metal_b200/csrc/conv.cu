@@ -12,6 +12,7 @@
 // Incremental (causal_conv1d.metal:50-82): conv over conv_state
 // (oldest..newest) and the current x, then shift-append x into the state.
 #include "common.cuh"
+#include "scan_math.cuh"
 
 namespace mb {
 
@@ -77,9 +78,122 @@ __global__ void conv1d_step_kernel(const T *__restrict__ x, int64_t xrs, const f
     for (int k = 0; k < K - 1; ++k) st[k] = win[k + 1];
 }
 
+
+// Vectorised full-sequence conv for channel-contiguous tensors: each thread
+// owns VEC = 16 / sizeof(T) adjacent channels (one 16-byte load per row)
+// and a run of kConvTC timesteps, loading kRows rows ahead so that enough
+// bytes are in flight per SM to cover HBM latency.
+template <typename T> struct Pack16;
+template <> struct Pack16<__half> {
+    static constexpr int kVec = 8;
+    static __device__ __forceinline__ void unpack(const uint4 &r, float *f) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 v = __half22float2(h[i]);
+            f[2 * i] = v.x;
+            f[2 * i + 1] = v.y;
+        }
+    }
+    static __device__ __forceinline__ uint4 pack(const float *f) {
+        uint4 r;
+        __half2 *h = reinterpret_cast<__half2 *>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        return r;
+    }
+};
+template <> struct Pack16<float> {
+    static constexpr int kVec = 4;
+    static __device__ __forceinline__ void unpack(const uint4 &r, float *f) {
+        f[0] = __uint_as_float(r.x);
+        f[1] = __uint_as_float(r.y);
+        f[2] = __uint_as_float(r.z);
+        f[3] = __uint_as_float(r.w);
+    }
+    static __device__ __forceinline__ uint4 pack(const float *f) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                          __float_as_uint(f[3]));
+    }
+};
+
+constexpr int kConvRows = 8;
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvCH)
+    conv1d_vec_kernel(const T *__restrict__ x, int64_t sx0, int64_t sx1, const float *__restrict__ w,
+                      const float *__restrict__ bias, T *__restrict__ y, int64_t sy0, int64_t sy1, int L, int D,
+                      int silu) {
+    constexpr int VEC = Pack16<T>::kVec;
+    constexpr bool PRECISE = sizeof(T) == 4;
+    const int d0 = (blockIdx.x * kConvCH + threadIdx.x) * VEC;
+    const int b = blockIdx.z;
+    const int t0 = blockIdx.y * kConvTC;
+    if (d0 >= D) return;
+    const int t1 = min(L, t0 + kConvTC);
+    float wk[K][VEC], bv[VEC];
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) wk[k][c] = w[(int64_t)(d0 + c) * K + k];
+        bv[c] = bias ? bias[d0 + c] : 0.f;
+    }
+    const T *xb = x + (int64_t)b * sx0 + d0;
+    T *yb = y + (int64_t)b * sy0 + d0;
+    float win[K][VEC];  // win[k] = x[t - K + 1 + k]
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int src = t0 - K + 1 + k;
+        if (src >= 0) {
+            const uint4 r = *reinterpret_cast<const uint4 *>(xb + (int64_t)src * sx1);
+            Pack16<T>::unpack(r, win[k]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) win[k][c] = 0.f;
+        }
+    }
+    for (int tb = t0; tb < t1; tb += kConvRows) {
+        uint4 raw[kConvRows];
+#pragma unroll
+        for (int r = 0; r < kConvRows; ++r)
+            if (tb + r < t1) raw[r] = *reinterpret_cast<const uint4 *>(xb + (int64_t)(tb + r) * sx1);
+#pragma unroll
+        for (int r = 0; r < kConvRows; ++r) {
+            if (tb + r >= t1) break;
+            Pack16<T>::unpack(raw[r], win[K - 1]);
+            float out[VEC];
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) {
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < K; ++k) acc = fmaf(win[k][c], wk[k][c], acc);
+                acc += bv[c];
+                if (silu) acc = PRECISE ? silu_f(acc) : silu_fast(acc);
+                out[c] = acc;
+            }
+            *reinterpret_cast<uint4 *>(yb + (int64_t)(tb + r) * sy1) = Pack16<T>::pack(out);
+#pragma unroll
+            for (int k = 0; k < K - 1; ++k)
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) win[k][c] = win[k + 1][c];
+        }
+    }
+}
+
 template <typename T, int K>
 int launch_conv_k(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
                   const int64_t *sy, int batch, int L, int D, int silu, cudaStream_t st) {
+    constexpr int VEC = Pack16<T>::kVec;
+    const bool vec = sx[2] == 1 && sy[2] == 1 && D % VEC == 0 &&
+                     reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                     (sx[1] * (int64_t)sizeof(T)) % 16 == 0 && (sy[1] * (int64_t)sizeof(T)) % 16 == 0 &&
+                     (sx[0] * (int64_t)sizeof(T)) % 16 == 0 && (sy[0] * (int64_t)sizeof(T)) % 16 == 0;
+    if (vec) {
+        dim3 grid(ceil_div(D / VEC, kConvCH), ceil_div(L, kConvTC), batch);
+        conv1d_vec_kernel<T, K><<<grid, kConvCH, 0, st>>>(static_cast<const T *>(x), sx[0], sx[1], w, bias,
+                                                           static_cast<T *>(y), sy[0], sy[1], L, D, silu);
+        return launch_status("causal_conv1d (vectorised) kernel");
+    }
     dim3 grid(ceil_div(D, kConvCH), ceil_div(L, kConvTC), batch);
     conv1d_kernel<T, K><<<grid, kConvCH, 0, st>>>(static_cast<const T *>(x), sx[0], sx[1], sx[2], w,
                                                    bias, static_cast<T *>(y), sy[0], sy[1], sy[2],

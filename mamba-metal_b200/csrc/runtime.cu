@@ -779,6 +779,8 @@ void mamba_destroy_state(MambaStateHandle *s) { delete s; }
 
 const char *mamba_last_error(void) { return mb::last_error(); }
 
+unsigned mamba_device_status(int clear) { return mb::device_error_flags(clear != 0); }
+
 int mamba_dt_rank(const MambaConfig *cfg) { return cfg ? (cfg->d_model + 15) / 16 : -1; }
 
 size_t mamba_weights_blob_size(const MambaConfig *cfg) {

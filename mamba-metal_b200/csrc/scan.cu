@@ -10,12 +10,18 @@
 //   y  = sum_n C[t,n] * h + D[d] * x,  then y *= SiLU(z) when a gate is given
 //
 // Decomposition.  One thread owns one (b, d) channel and keeps its N states
-// in registers; it walks time sequentially, so each (t, d, n) costs exactly
-// one exponential and no scan-operator overhead.  A CTA covers CH adjacent
-// channels of one batch row and one time chunk; per tile of TT timesteps the
-// CTA stages x, delta, z (CH channels wide) and B, C (shared by all channels)
-// in shared memory, so every global access is coalesced along whichever of
-// the channel or time axes is contiguous.
+// in registers; it walks time sequentially, so each (t, d, n) costs one
+// exponential and no scan-operator overhead.  A CTA covers CH = 128 adjacent
+// channels of one batch row and one time chunk.
+//
+// Staging.  When x, delta and z are channel-contiguous with 16-byte aligned
+// rows (the layout of the model's activations), a 4-stage TMA pipeline
+// brings [16 timesteps x 128 channels] tiles of each into shared memory
+// (cp.async.bulk.tensor, completion on an mbarrier), so the compute threads
+// issue no global loads for them; B and C (shared by every channel) are
+// prefetched one tile ahead through registers into an FP32 double buffer.
+// Any other layout goes through the generic kernel, which stages tiles with
+// cooperative loads along whichever axis is contiguous.
 //
 // When batch * ceil(D / CH) CTAs are too few to fill the GPU, time is split
 // into chunks (the carry propagation the reference intended in
@@ -25,16 +31,35 @@
 //            each chunk,
 //   phase 3  each chunk rescans from its entering state and writes y.
 // The same (P, H) monoid carries state across GPUs in sequence-sharded mode.
-#include "common.cuh"
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "scan_math.cuh"
+#include "tma.cuh"
 
 namespace mb {
 
+__device__ unsigned int g_device_error = 0;
+
 namespace {
 
-constexpr int kScanCH = 128;  // channels (= threads) per CTA
-constexpr int kScanTT = 32;   // timesteps per shared-memory tile
+constexpr int kScanCH = 128;    // channels (= threads) per CTA
+constexpr int kGenTT = 32;      // generic kernel: timesteps per tile
+#ifndef MAMBA_SCAN_TT
+#define MAMBA_SCAN_TT 8
+#endif
+#ifndef MAMBA_SCAN_STAGES
+#define MAMBA_SCAN_STAGES 6
+#endif
+constexpr int kTmaTT = MAMBA_SCAN_TT;          // TMA kernel: timesteps per tile
+constexpr int kTmaStages = MAMBA_SCAN_STAGES;  // TMA pipeline depth
+constexpr int kSubTT = 8;                      // generic kernel: timesteps per register batch
+constexpr int kChunkAlign = 32; // chunk lengths are multiples of both tile sizes
 
 enum ScanMode { kModeOutput = 0, kModeSummary = 1 };
 
@@ -49,18 +74,95 @@ struct ScanKParams {
     int64_t sx[3], sdt[3], sB[3], sC[3], sz[3], sy[3];
 };
 
-__device__ __forceinline__ float ex2_approx(float v) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
+// ---- shared per-tile loop ------------------------------------------------------
+// TT timesteps of one channel.  First the per-timestep scalars (softplus of
+// delta, SiLU of the gate) for the whole tile -- independent chains, so the
+// special-function pipe stays busy -- then the state recurrence, whose only
+// serial dependence between timesteps is one packed FMA per state pair.
+template <int NS, int CH, int TT, bool SUMMARY, bool PRECISE, bool SMALLA, int EMUL, typename Tx, typename Tdt>
+__device__ __forceinline__ void run_tile(const ScanKParams &p, int nt, int t0, int b, int d,
+                                         const Tx *__restrict__ sX, const Tdt *__restrict__ sDt,
+                                         const Tx *__restrict__ sZ, const float *__restrict__ sBC,
+                                         bool has_bias, float bias, float dskip, bool has_z, float2 *h,
+                                         const float2 *Ac, const float2 *kI, float2 *P) {
+    const int tid = threadIdx.x;
+    float dtv[TT], gv[TT];
+#pragma unroll
+    for (int tt = 0; tt < TT; ++tt) {
+        float draw = cvt_f32(sDt[tt * CH + tid]);
+        if (has_bias) draw = __fadd_rn(draw, bias);
+        dtv[tt] = scan_softplus<PRECISE>(draw);
+        gv[tt] = 1.f;
+        if (!SUMMARY && has_z) gv[tt] = scan_silu<PRECISE>(cvt_f32(sZ[tt * CH + tid]));
+    }
+    Tx *gy = static_cast<Tx *>(p.y) + (int64_t)b * p.sy[0] + (int64_t)t0 * p.sy[1] + (int64_t)d * p.sy[2];
+#pragma unroll
+    for (int tt = 0; tt < TT; ++tt) {
+        if (tt < nt) {
+            const float xv = cvt_f32(sX[tt * CH + tid]);
+            const float s = scan_step<NS, SUMMARY, PRECISE, SMALLA, EMUL>(xv, dtv[tt], sBC + tt * 2 * NS, h, Ac,
+                                                                          kI, P);
+            if (!SUMMARY) gy[(int64_t)tt * p.sy[1]] = cvt_out<Tx>(scan_output<PRECISE>(s, dskip, xv, gv[tt]));
+        }
+    }
 }
 
+// A tile of any length in sub-tiles of SUB timesteps.
+template <int NS, int CH, int SUB, bool SUMMARY, bool PRECISE, bool SMALLA, int EMUL, typename Tx, typename Tdt>
+__device__ __forceinline__ void run_steps(const ScanKParams &p, int nt, int t0, int b, int d,
+                                          const Tx *__restrict__ sX, const Tdt *__restrict__ sDt,
+                                          const Tx *__restrict__ sZ, const float *__restrict__ sBC,
+                                          bool has_bias, float bias, float dskip, bool has_z, float2 *h,
+                                          const float2 *Ac, const float2 *kI, float2 *P) {
+    for (int s0 = 0; s0 < nt; s0 += SUB)
+        run_tile<NS, CH, SUB, SUMMARY, PRECISE, SMALLA, EMUL>(
+            p, min(SUB, nt - s0), t0 + s0, b, d, sX + s0 * CH, sDt + s0 * CH, sZ + s0 * CH, sBC + s0 * 2 * NS,
+            has_bias, bias, dskip, has_z, h, Ac, kI, P);
+}
+
+// B and C of one tile as FP32 [TT][2*NS] (B[0..NS) then C[0..NS) per
+// timestep; zero beyond N, beyond the chunk, and C in summary mode).
+template <int NS, int CH, int TT, typename Tbc, bool SUMMARY>
+struct BCTile {
+    static constexpr int kElems = TT * 2 * NS;
+    static constexpr int kPer = (kElems + CH - 1) / CH;
+    float v[kPer];
+    __device__ __forceinline__ void load(const ScanKParams &p, int b, int t0, int t_end) {
+        const Tbc *gB = static_cast<const Tbc *>(p.B);
+        const Tbc *gC = static_cast<const Tbc *>(p.C);
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int e = threadIdx.x + i * CH;
+            float val = 0.f;
+            if (e < kElems) {
+                const int tt = e / (2 * NS), j = e % (2 * NS);
+                const int64_t t = t0 + tt;
+                if (t < t_end) {
+                    if (j < NS) {
+                        if (j < p.N) val = ld_f32(gB + (int64_t)b * p.sB[0] + t * p.sB[1] + (int64_t)j * p.sB[2]);
+                    } else if (!SUMMARY && j - NS < p.N) {
+                        val = ld_f32(gC + (int64_t)b * p.sC[0] + t * p.sC[1] + (int64_t)(j - NS) * p.sC[2]);
+                    }
+                }
+            }
+            v[i] = val;
+        }
+    }
+    __device__ __forceinline__ void store(float *dst) const {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int e = threadIdx.x + i * CH;
+            if (e < kElems) dst[e] = v[i];
+        }
+    }
+};
+
 // Stage a [TT, CH] tile of a per-channel tensor into shared memory (row tt,
-// column c).  Channel-contiguous tensors are read one row per warp pass;
+// column c).  Channel-contiguous tensors are read one row per pass;
 // otherwise consecutive threads read consecutive timesteps of one channel.
 template <typename T, int CH, int TT>
-__device__ __forceinline__ void stage_tile(T *s, const T *g, const int64_t *st, int b, int t0,
-                                           int nt, int d0, int D) {
+__device__ __forceinline__ void stage_tile(T *s, const T *g, const int64_t *st, int b, int t0, int nt,
+                                           int d0, int D) {
     const int tid = threadIdx.x;
     const T *gb = g + (int64_t)b * st[0];
     if (st[2] == 1) {
@@ -78,134 +180,222 @@ __device__ __forceinline__ void stage_tile(T *s, const T *g, const int64_t *st, 
     }
 }
 
+template <int NS>
+__device__ __forceinline__ void write_epilogue(const ScanKParams &p, bool summary, int b, int chunk, int d,
+                                               int t_end, const float2 *h, const float2 *P) {
+    const int N = p.N;
+    if (summary) {
+        const int64_t off = (((int64_t)b * p.nchunks + chunk) * p.D + d) * N;
+#pragma unroll
+        for (int q = 0; q < NS / 2; ++q) {
+            if (2 * q < N) {
+                p.sumP[off + 2 * q] = P[q].x;
+                p.sumH[off + 2 * q] = h[q].x;
+            }
+            if (2 * q + 1 < N) {
+                p.sumP[off + 2 * q + 1] = P[q].y;
+                p.sumH[off + 2 * q + 1] = h[q].y;
+            }
+        }
+    } else if (p.final_state && t_end == p.L) {
+        float *fs = p.final_state + ((int64_t)b * p.D + d) * N;
+#pragma unroll
+        for (int q = 0; q < NS / 2; ++q) {
+            if (2 * q < N) fs[2 * q] = h[q].x;
+            if (2 * q + 1 < N) fs[2 * q + 1] = h[q].y;
+        }
+    }
+}
+
+template <int NS>
+__device__ __forceinline__ void load_initial_state(const ScanKParams &p, int b, int chunk, int d, float2 *h,
+                                                   float2 *P) {
+#pragma unroll
+    for (int q = 0; q < NS / 2; ++q) {
+        h[q] = make_float2(0.f, 0.f);
+        P[q] = make_float2(1.f, 1.f);
+    }
+    if (p.h_init) {
+        const int N = p.N;
+        const float *src = p.h_init + (((int64_t)b * p.nchunks + chunk) * p.D + d) * N;
+#pragma unroll
+        for (int q = 0; q < NS / 2; ++q) {
+            if (2 * q < N) h[q].x = src[2 * q];
+            if (2 * q + 1 < N) h[q].y = src[2 * q + 1];
+        }
+    }
+}
+
+// ---- generic kernel (any strides) ------------------------------------------
 template <int NS, int CH, int TT, typename Tx, typename Tdt, typename Tbc, int MODE>
-__global__ void __launch_bounds__(CH) scan_kernel(const ScanKParams p) {
+__global__ void __launch_bounds__(CH) scan_generic_kernel(const ScanKParams p) {
+    constexpr bool PRECISE = std::is_same<Tx, float>::value;
+    constexpr bool SUMMARY = MODE == kModeSummary;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float *sB = reinterpret_cast<float *>(smem_raw);  // [TT][NS]
-    float *sC = sB + TT * NS;                          // [TT][NS]
-    Tx *sX = reinterpret_cast<Tx *>(sC + TT * NS);     // [TT][CH]
-    Tx *sZ = sX + TT * CH;                             // [TT][CH]
-    Tdt *sDt = reinterpret_cast<Tdt *>(sZ + TT * CH);  // [TT][CH]
+    float *sBC = reinterpret_cast<float *>(smem_raw);  // [TT][2*NS]
+    Tx *sX = reinterpret_cast<Tx *>(sBC + TT * 2 * NS);  // [TT][CH]
+    Tx *sZ = sX + TT * CH;                               // [TT][CH]
+    Tdt *sDt = reinterpret_cast<Tdt *>(sZ + TT * CH);    // [TT][CH]
 
     const int tid = threadIdx.x;
     const int b = blockIdx.z, chunk = blockIdx.y;
     const int d0 = blockIdx.x * CH, d = d0 + tid;
     const bool dvalid = d < p.D;
-    const int N = p.N;
     const int t_begin = chunk * p.chunk_len;
     const int t_end = min(p.L, t_begin + p.chunk_len);
 
-    float A2[NS], kI[NS], h[NS], P[NS];
-    bool small = false;
-#pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        const float a = (dvalid && n < N) ? p.A[(int64_t)d * N + n] : 0.f;
-        A2[n] = a * kLog2e;
-        const bool big = fabsf(a) > 1e-6f;
-        kI[n] = big ? 1.0f / a : 0.f;
-        small |= (dvalid && n < N && !big);
-        h[n] = 0.f;
-        P[n] = 1.f;
-    }
-    const int64_t st_off = (((int64_t)b * p.nchunks + chunk) * p.D + d) * N;
-    if (MODE == kModeOutput && p.h_init && dvalid) {
-#pragma unroll
-        for (int n = 0; n < NS; ++n)
-            if (n < N) h[n] = p.h_init[st_off + n];
-    }
+    float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
+    const bool small = load_channel_consts<NS, PRECISE>(p.A, d, p.N, dvalid, Ac, kI);
+    if (dvalid && !SUMMARY) load_initial_state<NS>(p, b, chunk, d, h, P);
+    else load_initial_state<NS>(ScanKParams{}, 0, 0, 0, h, P);
     const bool has_bias = p.dt_bias != nullptr;
     const float bias = (has_bias && dvalid) ? p.dt_bias[d] : 0.f;
     const float dskip = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const bool any_small = __syncthreads_or(small);
-    const bool has_z = (MODE == kModeOutput) && p.z != nullptr;
-
-    const Tx *gx = static_cast<const Tx *>(p.x);
-    const Tdt *gdt = static_cast<const Tdt *>(p.delta);
-    const Tx *gz = static_cast<const Tx *>(p.z);
-    const Tbc *gB = static_cast<const Tbc *>(p.B);
-    const Tbc *gC = static_cast<const Tbc *>(p.C);
-    Tx *gy = static_cast<Tx *>(p.y);
+    const bool has_z = !SUMMARY && p.z != nullptr;
 
     for (int t0 = t_begin; t0 < t_end; t0 += TT) {
         const int nt = min(TT, t_end - t0);
-        stage_tile<Tx, CH, TT>(sX, gx, p.sx, b, t0, nt, d0, p.D);
-        stage_tile<Tdt, CH, TT>(sDt, gdt, p.sdt, b, t0, nt, d0, p.D);
-        if (has_z) stage_tile<Tx, CH, TT>(sZ, gz, p.sz, b, t0, nt, d0, p.D);
-        for (int e = tid; e < TT * NS; e += CH) {
-            const int tt = e / NS, n = e % NS;
-            float bv = 0.f, cv = 0.f;
-            if (tt < nt && n < N) {
-                const int64_t t = t0 + tt;
-                bv = ld_f32(gB + (int64_t)b * p.sB[0] + t * p.sB[1] + (int64_t)n * p.sB[2]);
-                if (MODE == kModeOutput)
-                    cv = ld_f32(gC + (int64_t)b * p.sC[0] + t * p.sC[1] + (int64_t)n * p.sC[2]);
-            }
-            sB[e] = bv;
-            sC[e] = cv;
+        stage_tile<Tx, CH, TT>(sX, static_cast<const Tx *>(p.x), p.sx, b, t0, nt, d0, p.D);
+        stage_tile<Tdt, CH, TT>(sDt, static_cast<const Tdt *>(p.delta), p.sdt, b, t0, nt, d0, p.D);
+        if (has_z) stage_tile<Tx, CH, TT>(sZ, static_cast<const Tx *>(p.z), p.sz, b, t0, nt, d0, p.D);
+        {
+            BCTile<NS, CH, TT, Tbc, SUMMARY> bc;
+            bc.load(p, b, t0, t_end);
+            bc.store(sBC);
         }
         __syncthreads();
         if (dvalid) {
-            for (int tt = 0; tt < nt; ++tt) {
-                const float xv = cvt_f32(sX[tt * CH + tid]);
-                float draw = cvt_f32(sDt[tt * CH + tid]);
-                if (has_bias) draw = draw + bias;
-                const float dt = softplus_f(draw);
-                const float *Bt = sB + tt * NS;
-                const float *Ct = sC + tt * NS;
-                float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-                for (int n = 0; n < NS; ++n) {
-                    const float a = ex2_approx(dt * A2[n]);
-                    const float w = xv * Bt[n];
-                    float bb;
-                    if (any_small && kI[n] == 0.f) {
-                        bb = dt * w;
-                    } else {
-                        const float k = w * kI[n];
-                        bb = fmaf(a, k, -k);
-                    }
-                    h[n] = fmaf(a, h[n], bb);
-                    if (MODE == kModeSummary) {
-                        P[n] *= a;
-                    } else {
-                        if (n & 1) y1 = fmaf(Ct[n], h[n], y1);
-                        else y0 = fmaf(Ct[n], h[n], y0);
-                    }
-                }
-                if (MODE == kModeOutput) {
-                    float yv = fmaf(dskip, xv, y0 + y1);
-                    if (has_z) yv *= silu_f(cvt_f32(sZ[tt * CH + tid]));
-                    gy[(int64_t)b * p.sy[0] + (int64_t)(t0 + tt) * p.sy[1] + (int64_t)d * p.sy[2]] =
-                        cvt_out<Tx>(yv);
-                }
-            }
+            if (any_small)
+                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, true, 0>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
+                                                           dskip, has_z, h, Ac, kI, P);
+            else
+                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, false, 0>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
+                                                            dskip, has_z, h, Ac, kI, P);
         }
         __syncthreads();
     }
-
-    if (!dvalid) return;
-    if (MODE == kModeSummary) {
-#pragma unroll
-        for (int n = 0; n < NS; ++n)
-            if (n < N) {
-                p.sumP[st_off + n] = P[n];
-                p.sumH[st_off + n] = h[n];
-            }
-    } else if (p.final_state && t_end == p.L) {
-        float *fs = p.final_state + ((int64_t)b * p.D + d) * N;
-#pragma unroll
-        for (int n = 0; n < NS; ++n)
-            if (n < N) fs[n] = h[n];
-    }
+    if (dvalid) write_epilogue<NS>(p, SUMMARY, b, chunk, d, t_end, h, P);
 }
 
-// Phase 2: compose the chunk summaries of every (b, d, n) in time order.
-// On entry H/P hold the summaries [batch, nchunks, D*N]; when write_hin is
-// set, H is overwritten in place with the state entering each chunk.
+// ---- TMA-pipelined kernel (channel-contiguous, 16-byte aligned rows) ---------
+template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt>
+struct TmaLayout {
+    static constexpr int kXB = TT * CH * (int)sizeof(Tx);   // x or z tile bytes
+    static constexpr int kDB = TT * CH * (int)sizeof(Tdt);  // delta tile bytes
+    static constexpr int kStage = 2 * kXB + kDB;            // x | delta | z
+    static constexpr int kBC = 2 * TT * 2 * NS * 4;         // double-buffered FP32 B/C
+    static constexpr int kBytes = ST * kStage + kBC + ST * 8;
+    static_assert(kXB % 128 == 0 && kDB % 128 == 0, "TMA tiles must stay 128-byte aligned");
+};
+
+template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt, typename Tbc, int MODE, int EMUL>
+__global__ void __launch_bounds__(CH)
+    scan_tma_kernel(const ScanKParams p, const __grid_constant__ CUtensorMap tmx,
+                    const __grid_constant__ CUtensorMap tmdt, const __grid_constant__ CUtensorMap tmz) {
+    constexpr bool PRECISE = std::is_same<Tx, float>::value;
+    constexpr bool SUMMARY = MODE == kModeSummary;
+    using Lay = TmaLayout<NS, CH, TT, ST, Tx, Tdt>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);            // [2][TT][2*NS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ST * Lay::kStage + Lay::kBC);  // [ST]
+
+    const int tid = threadIdx.x;
+    const int b = blockIdx.z, chunk = blockIdx.y;
+    const int d0 = blockIdx.x * CH, d = d0 + tid;
+    const bool dvalid = d < p.D;
+    const int t_begin = chunk * p.chunk_len;
+    const int t_end = min(p.L, t_begin + p.chunk_len);
+    const int ntiles = t_end > t_begin ? (t_end - t_begin + TT - 1) / TT : 0;
+    const bool has_z = !SUMMARY && p.z != nullptr;
+    const uint32_t tx_bytes = Lay::kXB + Lay::kDB + (has_z ? Lay::kXB : 0);
+
+    float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
+    const bool small = load_channel_consts<NS, PRECISE>(p.A, d, p.N, dvalid, Ac, kI);
+    if (dvalid && !SUMMARY) load_initial_state<NS>(p, b, chunk, d, h, P);
+    else load_initial_state<NS>(ScanKParams{}, 0, 0, 0, h, P);
+    const bool has_bias = p.dt_bias != nullptr;
+    const float bias = (has_bias && dvalid) ? p.dt_bias[d] : 0.f;
+    const float dskip = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
+
+    if (tid == 0) {
+        prefetch_tensormap(&tmx);
+        prefetch_tensormap(&tmdt);
+        if (has_z) prefetch_tensormap(&tmz);
+        for (int s = 0; s < ST; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    const bool any_small = __syncthreads_or(small);
+
+    auto issue = [&](int tile, int s) {
+        unsigned char *stg = smem + s * Lay::kStage;
+        const int t = t_begin + tile * TT;
+        mbar_arrive_expect_tx(&bars[s], tx_bytes);
+        tma_load_3d(stg, &tmx, &bars[s], d0, t, b);
+        tma_load_3d(stg + Lay::kXB, &tmdt, &bars[s], d0, t, b);
+        if (has_z) tma_load_3d(stg + Lay::kXB + Lay::kDB, &tmz, &bars[s], d0, t, b);
+    };
+    if (tid == 0)
+        for (int s = 0; s < min(ST, ntiles); ++s) issue(s, s);
+
+    BCTile<NS, CH, TT, Tbc, SUMMARY> bc;
+    if (ntiles > 0) {
+        bc.load(p, b, t_begin, t_end);
+        bc.store(bcf);
+    }
+    __syncthreads();
+
+    int i = 0;
+    bool aborted = false;
+    for (; i < ntiles; ++i) {
+        const int s = i % ST;
+        const int t0 = t_begin + i * TT;
+        const int nt = min(TT, t_end - t0);
+        if (i + 1 < ntiles) bc.load(p, b, t0 + TT, t_end);
+        const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((i / ST) & 1));
+        if (ok && dvalid) {
+            const unsigned char *stg = smem + s * Lay::kStage;
+            const Tx *sX = reinterpret_cast<const Tx *>(stg);
+            const Tdt *sDt = reinterpret_cast<const Tdt *>(stg + Lay::kXB);
+            const Tx *sZ = reinterpret_cast<const Tx *>(stg + Lay::kXB + Lay::kDB);
+            const float *sBC = bcf + (i & 1) * TT * 2 * NS;
+            if (any_small)
+                run_tile<NS, CH, TT, SUMMARY, PRECISE, true, EMUL>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
+                                                              dskip, has_z, h, Ac, kI, P);
+            else
+                run_tile<NS, CH, TT, SUMMARY, PRECISE, false, EMUL>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                                                               bias, dskip, has_z, h, Ac, kI, P);
+        }
+        if (i + 1 < ntiles) bc.store(bcf + ((i + 1) & 1) * TT * 2 * NS);
+        // One barrier per tile: the stage and the B/C buffer are free again,
+        // and a timed-out wait anywhere in the CTA aborts all of it.
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            break;
+        }
+        if (tid == 0 && i + ST < ntiles) issue(i + ST, s);
+    }
+    if (aborted) {
+        if (tid == 0) {
+            atomicOr(&g_device_error, kErrTmaTimeout);
+            // Let copies still in flight into this CTA's shared memory land
+            // (each wait bounded) before the CTA exits.
+            for (int j = i; j < min(i + ST, ntiles); ++j)
+                mbar_wait_bounded(&bars[j % ST], (uint32_t)((j / ST) & 1));
+        }
+        __syncthreads();
+        return;
+    }
+    if (dvalid) write_epilogue<NS>(p, SUMMARY, b, chunk, d, t_end, h, P);
+}
+
+// ---- phase 2 and the cross-rank composition -----------------------------------
+// Compose the chunk summaries of every (b, d, n) in time order.  On entry
+// H/P hold the summaries [batch, nchunks, D*N]; when write_hin is set, H is
+// overwritten in place with the state entering each chunk.
 __global__ void scan_combine_kernel(const float *__restrict__ P, float *__restrict__ H,
-                                    const float *__restrict__ h0, int nchunks, int64_t DN,
-                                    int64_t total, int write_hin, float *__restrict__ P_total,
-                                    float *__restrict__ H_total) {
+                                    const float *__restrict__ h0, int nchunks, int64_t DN, int64_t total,
+                                    int write_hin, float *__restrict__ P_total, float *__restrict__ H_total) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= total) return;
     const int64_t b = i / DN, r = i % DN;
@@ -222,8 +412,7 @@ __global__ void scan_combine_kernel(const float *__restrict__ P, float *__restri
     if (P_total) P_total[i] = pt;
 }
 
-// Sequence-sharded mode: state entering rank `rank` from the gathered
-// per-rank summaries PH[world][2][count].
+// State entering rank `rank` from the gathered summaries PH[world][2][count].
 __global__ void scan_compose_prefix_kernel(const float *__restrict__ PH, int rank, int64_t count,
                                            const float *__restrict__ h0, float *__restrict__ h_in) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -236,34 +425,117 @@ __global__ void scan_compose_prefix_kernel(const float *__restrict__ PH, int ran
     h_in[i] = h;
 }
 
+// ---- host side ------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 3-D map over a [batch, L, D] tensor with channel stride 1; box
+// [1, TT, CH].  False when the layout does not meet the TMA rules (16-byte
+// aligned base and strides), in which case the generic kernel is used.
+bool encode_map(CUtensorMap *m, const void *ptr, int dtype, int D, int L, int B, const int64_t *st) {
+    auto fn = tensor_map_encoder();
+    if (!fn || !ptr || st[2] != 1) return false;
+    const int64_t es = dtype == MAMBA_F16 ? 2 : 4;
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    const int64_t row = st[1] * es;
+    int64_t bat = st[0] * es;
+    if (row <= 0 || row % 16 || row < D * es) return false;
+    if (B == 1) bat = row * std::max(L, 1);
+    if (bat <= 0 || bat % 16) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)row, (cuuint64_t)bat};
+    cuuint32_t box[3] = {(cuuint32_t)kScanCH, (cuuint32_t)kTmaTT, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, dtype == MAMBA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          3, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Number of fast-path states whose exponential runs on the FMA pipe
+// (tuning knob MAMBA_SCAN_EMUL in {0, 2, 4, 6, 8}; default 0).
+int emul_setting() {
+    static int v = [] {
+        const char *e = std::getenv("MAMBA_SCAN_EMUL");
+        const int x = e ? std::atoi(e) : 0;
+        return (x == 2 || x == 4 || x == 6 || x == 8) ? x : 0;
+    }();
+    return v;
+}
+
+template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE, int EMUL>
+int launch_tma(const ScanKParams &kp, const CUtensorMap &mx, const CUtensorMap &mdt, const CUtensorMap &mz,
+               cudaStream_t st) {
+    constexpr int CH = kScanCH, TT = kTmaTT, ST = kTmaStages;
+    auto kern = scan_tma_kernel<NS, CH, TT, ST, Tx, Tdt, Tbc, MODE, EMUL>;
+    const int smem = TmaLayout<NS, CH, TT, ST, Tx, Tdt>::kBytes;
+    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    dim3 grid(ceil_div(kp.D, CH), kp.nchunks, kp.batch);
+    kern<<<grid, CH, smem, st>>>(kp, mx, mdt, mz);
+    return launch_status("selective_scan (TMA) kernel");
+}
+
 template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE>
-int launch_scan(const ScanKParams &kp, cudaStream_t st) {
-    constexpr int CH = kScanCH, TT = kScanTT;
-    auto kern = scan_kernel<NS, CH, TT, Tx, Tdt, Tbc, MODE>;
-    const size_t smem = (size_t)TT * NS * 4 * 2 + (size_t)TT * CH * (2 * sizeof(Tx) + sizeof(Tdt));
+int launch_generic(const ScanKParams &kp, cudaStream_t st) {
+    constexpr int CH = kScanCH, TT = kGenTT;
+    auto kern = scan_generic_kernel<NS, CH, TT, Tx, Tdt, Tbc, MODE>;
+    const size_t smem = (size_t)TT * 2 * NS * 4 + (size_t)TT * CH * (2 * sizeof(Tx) + sizeof(Tdt));
     MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(ceil_div(kp.D, CH), kp.nchunks, kp.batch);
     kern<<<grid, CH, smem, st>>>(kp);
     return launch_status("selective_scan kernel");
 }
 
+template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE>
+int launch_scan_ns(const ScanKParams &kp, int xd, int dd, cudaStream_t st) {
+    CUtensorMap mx, mdt, mz;
+    const bool want_z = MODE == kModeOutput && kp.z != nullptr;
+    const bool tma = kp.L > 0 && encode_map(&mx, kp.x, xd, kp.D, kp.L, kp.batch, kp.sx) &&
+                     encode_map(&mdt, kp.delta, dd, kp.D, kp.L, kp.batch, kp.sdt) &&
+                     (!want_z || encode_map(&mz, kp.z, xd, kp.D, kp.L, kp.batch, kp.sz));
+    if (!tma) return launch_generic<NS, Tx, Tdt, Tbc, MODE>(kp, st);
+    if (!want_z) mz = mx;  // unused by the kernel
+    if (!std::is_same<Tx, float>::value && MODE == kModeOutput && NS == 16) {
+        switch (emul_setting()) {
+            case 2: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 2>(kp, mx, mdt, mz, st);
+            case 4: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 4>(kp, mx, mdt, mz, st);
+            case 6: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 6>(kp, mx, mdt, mz, st);
+            case 8: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 8>(kp, mx, mdt, mz, st);
+            default: break;
+        }
+    }
+    return launch_tma<NS, Tx, Tdt, Tbc, MODE, 0>(kp, mx, mdt, mz, st);
+}
+
 template <typename Tx, typename Tdt, typename Tbc, int MODE>
-int launch_scan_ns(const ScanKParams &kp, cudaStream_t st) {
-    if (kp.N <= 4) return launch_scan<4, Tx, Tdt, Tbc, MODE>(kp, st);
-    if (kp.N <= 8) return launch_scan<8, Tx, Tdt, Tbc, MODE>(kp, st);
-    return launch_scan<16, Tx, Tdt, Tbc, MODE>(kp, st);
+int launch_scan_n(const ScanKParams &kp, int xd, int dd, cudaStream_t st) {
+    if (kp.N <= 4) return launch_scan_ns<4, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
+    if (kp.N <= 8) return launch_scan_ns<8, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
+    return launch_scan_ns<16, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
 }
 
 template <int MODE>
 int launch_scan_dtypes(const ScanKParams &kp, int xd, int dd, int bd, cudaStream_t st) {
     if (xd == MAMBA_F32 && dd == MAMBA_F32 && bd == MAMBA_F32)
-        return launch_scan_ns<float, float, float, MODE>(kp, st);
+        return launch_scan_n<float, float, float, MODE>(kp, xd, dd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F16 && bd == MAMBA_F16)
-        return launch_scan_ns<__half, __half, __half, MODE>(kp, st);
+        return launch_scan_n<__half, __half, __half, MODE>(kp, xd, dd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F16)
-        return launch_scan_ns<__half, float, __half, MODE>(kp, st);
+        return launch_scan_n<__half, float, __half, MODE>(kp, xd, dd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F32)
-        return launch_scan_ns<__half, float, float, MODE>(kp, st);
+        return launch_scan_n<__half, float, float, MODE>(kp, xd, dd, st);
     set_error("selective_scan: unsupported dtype combination (x, delta, B/C)");
     return -1;
 }
@@ -274,7 +546,7 @@ int launch_scan_dtypes(const ScanKParams &kp, int xd, int dd, int bd, cudaStream
 int choose_chunk_len(int batch, int L, int D, int requested) {
     if (L <= 0) return 1;
     if (requested > 0) {
-        const int c = ceil_div(requested, kScanTT) * kScanTT;
+        const int c = ceil_div(requested, kChunkAlign) * kChunkAlign;
         return std::min(c, L);
     }
     const int64_t ctas = (int64_t)batch * ceil_div(D, kScanCH);
@@ -284,7 +556,7 @@ int choose_chunk_len(int batch, int L, int D, int requested) {
     const int64_t maxc = std::max<int64_t>(1, L / 128);
     const int64_t nc = std::min(want, maxc);
     if (nc <= 1) return L;
-    const int clen = (int)(ceil_div64(ceil_div64(L, nc), kScanTT) * kScanTT);
+    const int clen = (int)(ceil_div64(ceil_div64(L, nc), kChunkAlign) * kChunkAlign);
     return std::min(clen, L);
 }
 
@@ -330,13 +602,13 @@ ScanKParams make_params(const MambaScanArgs *a, int chunk_len) {
     return kp;
 }
 
-int launch_combine(const float *P, float *H, const float *h0, int nchunks, int64_t DN, int batch,
-                   int write_hin, float *P_total, float *H_total, cudaStream_t st) {
+int launch_combine(const float *P, float *H, const float *h0, int nchunks, int64_t DN, int batch, int write_hin,
+                   float *P_total, float *H_total, cudaStream_t st) {
     const int64_t total = (int64_t)batch * DN;
     if (total == 0) return 0;
     const int threads = 256;
-    scan_combine_kernel<<<(unsigned)ceil_div64(total, threads), threads, 0, st>>>(
-        P, H, h0, nchunks, DN, total, write_hin, P_total, H_total);
+    scan_combine_kernel<<<(unsigned)ceil_div64(total, threads), threads, 0, st>>>(P, H, h0, nchunks, DN, total,
+                                                                                 write_hin, P_total, H_total);
     return launch_status("scan_combine kernel");
 }
 
@@ -369,14 +641,12 @@ int selective_scan(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream
     k1.sumP = sumP;
     k1.sumH = sumH;
     if (launch_scan_dtypes<kModeSummary>(k1, a->x_dtype, a->delta_dtype, a->bc_dtype, st)) return -1;
-    if (launch_combine(sumP, sumH, a->initial_state, kp.nchunks, DN, a->batch, 1, nullptr, nullptr, st))
-        return -1;
+    if (launch_combine(sumP, sumH, a->initial_state, kp.nchunks, DN, a->batch, 1, nullptr, nullptr, st)) return -1;
     kp.h_init = sumH;
     return launch_scan_dtypes<kModeOutput>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st);
 }
 
-int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws_bytes,
-                 cudaStream_t st) {
+int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws_bytes, cudaStream_t st) {
     if (validate(a)) return -1;
     if (a->batch == 0 || a->dim == 0) return 0;
     MB_CHECK_ARG(P && H, "scan_summary: P and H are required");
@@ -403,15 +673,25 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
     return launch_combine(sumP, sumH, nullptr, kp.nchunks, DN, a->batch, 0, P, H, st);
 }
 
-int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
-                        float *h_in, cudaStream_t st) {
+int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0, float *h_in,
+                        cudaStream_t st) {
     MB_CHECK_ARG(PH && h_in, "scan_compose_prefix: null buffer");
     MB_CHECK_ARG(world >= 1 && rank >= 0 && rank < world, "scan_compose_prefix: bad rank");
     if (count <= 0) return 0;
     const int threads = 256;
-    scan_compose_prefix_kernel<<<(unsigned)ceil_div64(count, threads), threads, 0, st>>>(
-        PH, rank, count, h0, h_in);
+    scan_compose_prefix_kernel<<<(unsigned)ceil_div64(count, threads), threads, 0, st>>>(PH, rank, count, h0,
+                                                                                          h_in);
     return launch_status("scan_compose_prefix kernel");
+}
+
+unsigned device_error_flags(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return ~0u;
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    }
+    return v;
 }
 
 }  // namespace mb

@@ -5,22 +5,19 @@
 //   dt = softplus(delta + dt_bias)
 //   h[n] = exp(dt*A[d,n]) * h[n] + (exp(dt*A)-1)/A * B[n] * x
 //   y = (sum_n C[n]*h[n] + D*x) * SiLU(z)
-// One thread per (b, d); its N FP32 states are a contiguous 64-byte run, so
-// a warp reads and writes 2 KB of state with 16-byte vector accesses.  The
-// arithmetic is the same sequence the full-sequence scan uses, so T decode
-// steps reproduce a T-token forward.  HBM-bound on the state read-modify-
-// write (8*N bytes per (b,d)).
+// One thread per (b, d); its N FP32 states are a contiguous run, so a warp
+// reads and writes 2 KB of state with 16-byte vector accesses.  The update
+// is the same scan_step the full-sequence scan runs, so T decode steps
+// reproduce a T-token forward.  HBM-bound on the state read-modify-write
+// (8*N bytes per (b, d)).
+#include <type_traits>
+
 #include "common.cuh"
+#include "scan_math.cuh"
 
 namespace mb {
 
 namespace {
-
-__device__ __forceinline__ float ex2_approx(float v) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
-}
 
 template <int NS, typename Tx, typename Tdt, typename Tbc>
 __global__ void __launch_bounds__(128)
@@ -29,66 +26,60 @@ __global__ void __launch_bounds__(128)
                     const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
                     const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
                     Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N) {
-    __shared__ float sB[NS], sC[NS];
+    constexpr bool PRECISE = std::is_same<Tx, float>::value;
+    __shared__ __align__(16) float sBC[2 * NS];  // B[0..NS) then C[0..NS)
     const int b = blockIdx.y;
     const int d = blockIdx.x * blockDim.x + threadIdx.x;
-    if (threadIdx.x < NS) {
-        const int n = threadIdx.x;
-        sB[n] = n < N ? ld_f32(Bm + (int64_t)b * bcrs + n) : 0.f;
-        sC[n] = n < N ? ld_f32(Cm + (int64_t)b * bcrs + n) : 0.f;
+    if (threadIdx.x < 2 * NS) {
+        const int j = threadIdx.x;
+        float v = 0.f;
+        if (j < NS) {
+            if (j < N) v = ld_f32(Bm + (int64_t)b * bcrs + j);
+        } else if (j - NS < N) {
+            v = ld_f32(Cm + (int64_t)b * bcrs + (j - NS));
+        }
+        sBC[j] = v;
     }
     __syncthreads();
     if (d >= D) return;
-    const float xv = ld_f32(x + (int64_t)b * xrs + d);
-    float draw = ld_f32(delta + (int64_t)b * drs + d);
-    if (dt_bias) draw = draw + dt_bias[d];
-    const float dt = softplus_f(draw);
+    float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
+    const bool small = load_channel_consts<NS, PRECISE>(A, d, N, true, Ac, kI);
     float *hp = state + ((int64_t)b * D + d) * N;
-    float h[NS];
     const bool vec = (NS == N) && (NS % 4 == 0);
     if (vec) {
 #pragma unroll
         for (int i = 0; i < NS / 4; ++i) {
             const float4 v = reinterpret_cast<const float4 *>(hp)[i];
-            h[4 * i] = v.x;
-            h[4 * i + 1] = v.y;
-            h[4 * i + 2] = v.z;
-            h[4 * i + 3] = v.w;
+            h[2 * i] = make_float2(v.x, v.y);
+            h[2 * i + 1] = make_float2(v.z, v.w);
         }
     } else {
 #pragma unroll
-        for (int n = 0; n < NS; ++n) h[n] = n < N ? hp[n] : 0.f;
-    }
-    float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        const float a_c = n < N ? A[(int64_t)d * N + n] : 0.f;
-        const float a = ex2_approx(dt * (a_c * kLog2e));
-        const float w = xv * sB[n];
-        float bb;
-        if (fabsf(a_c) > 1e-6f) {
-            const float k = w * (1.0f / a_c);
-            bb = fmaf(a, k, -k);
-        } else {
-            bb = dt * w;
+        for (int q = 0; q < NS / 2; ++q) {
+            h[q].x = 2 * q < N ? hp[2 * q] : 0.f;
+            h[q].y = 2 * q + 1 < N ? hp[2 * q + 1] : 0.f;
         }
-        h[n] = fmaf(a, h[n], bb);
-        if (n & 1) y1 = fmaf(sC[n], h[n], y1);
-        else y0 = fmaf(sC[n], h[n], y0);
     }
+    const float xv = ld_f32(x + (int64_t)b * xrs + d);
+    float draw = ld_f32(delta + (int64_t)b * drs + d);
+    if (dt_bias) draw = __fadd_rn(draw, dt_bias[d]);
+    const float dt = scan_softplus<PRECISE>(draw);
+    const float s = small ? scan_step<NS, false, PRECISE, true, 0>(xv, dt, sBC, h, Ac, kI, P)
+                          : scan_step<NS, false, PRECISE, false, 0>(xv, dt, sBC, h, Ac, kI, P);
     if (vec) {
 #pragma unroll
         for (int i = 0; i < NS / 4; ++i)
-            reinterpret_cast<float4 *>(hp)[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+            reinterpret_cast<float4 *>(hp)[i] = make_float4(h[2 * i].x, h[2 * i].y, h[2 * i + 1].x, h[2 * i + 1].y);
     } else {
 #pragma unroll
-        for (int n = 0; n < NS; ++n)
-            if (n < N) hp[n] = h[n];
+        for (int q = 0; q < NS / 2; ++q) {
+            if (2 * q < N) hp[2 * q] = h[q].x;
+            if (2 * q + 1 < N) hp[2 * q + 1] = h[q].y;
+        }
     }
     const float dsk = Dskip ? Dskip[d] : 0.f;
-    float yv = fmaf(dsk, xv, y0 + y1);
-    if (z) yv *= silu_f(ld_f32(z + (int64_t)b * zrs + d));
-    y[(int64_t)b * yrs + d] = cvt_out<Tx>(yv);
+    const float gate = z ? scan_silu<PRECISE>(ld_f32(z + (int64_t)b * zrs + d)) : 1.f;
+    y[(int64_t)b * yrs + d] = cvt_out<Tx>(scan_output<PRECISE>(s, dsk, xv, gate));
 }
 
 template <int NS, typename Tx, typename Tdt, typename Tbc>

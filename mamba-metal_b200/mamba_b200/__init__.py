@@ -24,7 +24,9 @@ import struct
 import numpy as np
 
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libmamba_b200.so")
+# MAMBA_B200_LIB selects another build of the same library (e.g. a tuning
+# variant); by default the in-tree build is loaded.
+LIB_PATH = os.environ.get("MAMBA_B200_LIB") or os.path.join(PKG_DIR, "lib", "libmamba_b200.so")
 
 F32 = 0
 F16 = 1
@@ -78,6 +80,7 @@ _PROTOTYPES = {
     "mamba_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "mamba_destroy_state": (None, [c_void_p]),
     "mamba_last_error": (ctypes.c_char_p, []),
+    "mamba_device_status": (ctypes.c_uint, [c_int]),
     "mamba_dt_rank": (c_int, [ctypes.POINTER(MambaConfig)]),
     "mamba_weights_blob_size": (c_size, [ctypes.POINTER(MambaConfig)]),
     "mamba_init_weights_random": (c_int, [c_void_p, ctypes.c_uint64]),
@@ -138,6 +141,11 @@ def _check(rc, what):
 
 def last_error():
     return lib().mamba_last_error().decode()
+
+
+def device_status(clear=True):
+    """Kernel error flags on the current device (0 = none)."""
+    return lib().mamba_device_status(int(clear))
 
 
 # ---------------------------------------------------------------------------

@@ -188,35 +188,41 @@ def causal_conv1d(x, w, bias=None, silu=True):
 
 def causal_conv1d_step(x_t, w, bias, conv_state, silu=True):
     """x_t [batch, D]; conv_state [batch, D, K-1] FP32 updated in place."""
+    # Every array handed to C by address stays bound to a local name until
+    # the call returns (a temporary would be freed before the call runs).
     x_t = _f32(x_t)
+    w = _f32(w)
+    bias = None if bias is None else _f32(bias)
     bsz, D = x_t.shape
     K = w.shape[1]
     y = np.empty((bsz, D), np.float32)
     assert conv_state.dtype == np.float32 and conv_state.flags.c_contiguous
-    lib().oracle_causal_conv1d_step(_ptr(x_t), _ptr(_f32(w)), _ptr(None if bias is None else _f32(bias)),
-                                    _ptr(y), _ptr(conv_state), bsz, D, K, int(silu))
+    lib().oracle_causal_conv1d_step(_ptr(x_t), _ptr(w), _ptr(bias), _ptr(y), _ptr(conv_state),
+                                    bsz, D, K, int(silu))
     return y
 
 
 def ssm_step(x, delta, B, C, A, Dskip, state, z=None, dt_bias=None):
     """x, delta, z [batch, D]; B, C [batch, N]; state [batch, D, N] in place."""
-    x, delta, B, C = map(_f32, (x, delta, B, C))
+    x, delta, B, C, A, Dskip = map(_f32, (x, delta, B, C, A, Dskip))
+    z = None if z is None else _f32(z)
+    dt_bias = None if dt_bias is None else _f32(dt_bias)
     bsz, D = x.shape
     N = A.shape[1]
     y = np.empty((bsz, D), np.float32)
     assert state.dtype == np.float32 and state.flags.c_contiguous
-    lib().oracle_ssm_step(_ptr(x), _ptr(delta), _ptr(None if dt_bias is None else _f32(dt_bias)),
-                          _ptr(B), _ptr(C), B.strides[0] // 4, C.strides[0] // 4, _ptr(_f32(A)),
-                          _ptr(_f32(Dskip)), _ptr(None if z is None else _f32(z)), _ptr(y),
-                          _ptr(state), bsz, D, N)
+    lib().oracle_ssm_step(_ptr(x), _ptr(delta), _ptr(dt_bias), _ptr(B), _ptr(C), B.strides[0] // 4,
+                          C.strides[0] // 4, _ptr(A), _ptr(Dskip), _ptr(z), _ptr(y), _ptr(state),
+                          bsz, D, N)
     return y
 
 
 def rmsnorm(x, w=None, eps=1e-5):
     x = _f32(x)
+    w = None if w is None else _f32(w)
     rows, cols = x.shape
     y = np.empty_like(x)
-    lib().oracle_rmsnorm(_ptr(x), _ptr(None if w is None else _f32(w)), _ptr(y), rows, cols, eps)
+    lib().oracle_rmsnorm(_ptr(x), _ptr(w), _ptr(y), rows, cols, eps)
     return y
 
 
