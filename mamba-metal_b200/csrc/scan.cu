@@ -15,8 +15,8 @@
 // channels of one batch row and one time chunk.
 //
 // Staging.  When x, delta and z are channel-contiguous with 16-byte aligned
-// rows (the layout of the model's activations), a 4-stage TMA pipeline
-// brings [16 timesteps x 128 channels] tiles of each into shared memory
+// rows (the layout of the model's activations), a 6-stage TMA pipeline
+// brings [8 timesteps x 128 channels] tiles of each into shared memory
 // (cp.async.bulk.tensor, completion on an mbarrier), so the compute threads
 // issue no global loads for them; B and C (shared by every channel) are
 // prefetched one tile ahead through registers into an FP32 double buffer.
@@ -34,7 +34,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -463,17 +462,6 @@ bool encode_map(CUtensorMap *m, const void *ptr, int dtype, int D, int L, int B,
     return r == CUDA_SUCCESS;
 }
 
-// Number of fast-path states whose exponential runs on the FMA pipe
-// (tuning knob MAMBA_SCAN_EMUL in {0, 2, 4, 6, 8}; default 0).
-int emul_setting() {
-    static int v = [] {
-        const char *e = std::getenv("MAMBA_SCAN_EMUL");
-        const int x = e ? std::atoi(e) : 0;
-        return (x == 2 || x == 4 || x == 6 || x == 8) ? x : 0;
-    }();
-    return v;
-}
-
 template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE, int EMUL>
 int launch_tma(const ScanKParams &kp, const CUtensorMap &mx, const CUtensorMap &mdt, const CUtensorMap &mz,
                cudaStream_t st) {
@@ -507,15 +495,6 @@ int launch_scan_ns(const ScanKParams &kp, int xd, int dd, cudaStream_t st) {
                      (!want_z || encode_map(&mz, kp.z, xd, kp.D, kp.L, kp.batch, kp.sz));
     if (!tma) return launch_generic<NS, Tx, Tdt, Tbc, MODE>(kp, st);
     if (!want_z) mz = mx;  // unused by the kernel
-    if (!std::is_same<Tx, float>::value && MODE == kModeOutput && NS == 16) {
-        switch (emul_setting()) {
-            case 2: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 2>(kp, mx, mdt, mz, st);
-            case 4: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 4>(kp, mx, mdt, mz, st);
-            case 6: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 6>(kp, mx, mdt, mz, st);
-            case 8: return launch_tma<NS, Tx, Tdt, Tbc, MODE, 8>(kp, mx, mdt, mz, st);
-            default: break;
-        }
-    }
     return launch_tma<NS, Tx, Tdt, Tbc, MODE, 0>(kp, mx, mdt, mz, st);
 }
 
