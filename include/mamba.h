@@ -217,6 +217,26 @@ size_t mamba_selective_scan_workspace(const MambaScanArgs *a);
 int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes,
                          void *stream);
 
+/* The fused selective scan without a caller workspace: it allocates no
+ * device memory (no cudaMalloc, cudaFree or allocating library call).  No
+ * counterpart in the reference.  For callers that cannot allocate device
+ * memory or pass scratch to us: hosts whose interface has no slot for a
+ * workspace pointer (for instance ones that bind only the Metal kernels'
+ * buffer list), and processes that fix their device-memory budget at start-up
+ * and forbid allocations afterwards.  When the sequence is split into time
+ * chunks, the chunk carries live in one static 32 MiB array in the library's
+ * device globals, which every GPU that loads the library holds until the
+ * process exits; args needing more than that (see
+ * mamba_selective_scan_workspace) are rejected with -1 and a message.  The
+ * first call on a device looks up that array's address (once per device), so
+ * make that first call before any stream capture.  All calls share the one
+ * array and nothing in it carries over between calls (every slot a call reads
+ * is written earlier by the same call), but calls that overlap on the GPU
+ * (other streams, other host threads on the same device) race on it:
+ * serialise them.  Results equal mamba_selective_scan's for the same args.
+ * 0 / -1. */
+int mamba_selective_scan_noalloc(const MambaScanArgs *a, void *stream);
+
 /* Sequence-sharded mode, step 1: summary of this rank's slice of the
  * sequence: for every (b, d, n) the affine map h -> P*h + H that the slice
  * applies to its incoming state.  P, H: DEVICE FP32 [batch, dim, dstate].

@@ -17,6 +17,7 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
 int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
                         float *h_in, cudaStream_t st);
 unsigned device_error_flags(bool clear);
+int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st);
 
 // conv.cu
 int causal_conv1d(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,

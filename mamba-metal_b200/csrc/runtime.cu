@@ -892,6 +892,11 @@ int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspa
     return mb::selective_scan(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) ? -1 : 0;
 }
 
+int mamba_selective_scan_noalloc(const MambaScanArgs *a, void *stream) {
+    mb::clear_error();
+    return mb::selective_scan_noalloc(a, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
 int mamba_scan_summary(const MambaScanArgs *a, float *P, float *H, void *workspace, size_t workspace_bytes,
                        void *stream) {
     mb::clear_error();

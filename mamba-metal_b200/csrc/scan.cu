@@ -35,7 +35,9 @@
 
 #include <algorithm>
 #include <mutex>
+#include <string>
 #include <type_traits>
+#include <vector>
 
 #include "common.cuh"
 #include "scan_math.cuh"
@@ -661,6 +663,52 @@ int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, con
     scan_compose_prefix_kernel<<<(unsigned)ceil_div64(count, threads), threads, 0, st>>>(PH, rank, count, h0,
                                                                                           h_in);
     return launch_status("scan_compose_prefix kernel");
+}
+
+// ---- no-allocation entry point ------------------------------------------------
+// Scratch for mamba_selective_scan_noalloc: a fixed 32 MiB array in the
+// module's global memory.  Every device that loads this library holds it
+// until the process exits.  In host code `g_noalloc_scratch` is only a
+// host-side stand-in for the symbol, so its device address is looked up once
+// per device with cudaGetSymbolAddress and that address is what the kernels
+// receive.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device (resolved on the
+// first call on each device, with that device current).
+int noalloc_scratch(void **out) {
+    static std::mutex mu;
+    static std::vector<void *> cache;
+    int dev = 0;
+    MB_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
+    if (!cache[dev]) {
+        void *p = nullptr;
+        MB_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        cache[dev] = p;
+    }
+    *out = cache[dev];
+    return 0;
+}
+
+}  // namespace
+
+int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st) {
+    if (validate(a)) return -1;
+    const size_t need = scan_workspace_bytes(a);
+    if (need > kNoAllocScratchBytes) {
+        set_error("selective_scan_noalloc: these sizes need " + std::to_string(need) +
+                  " bytes of scratch, above the static maximum of " + std::to_string(kNoAllocScratchBytes) +
+                  " bytes; call mamba_selective_scan with a workspace instead");
+        return -1;
+    }
+    void *ws = nullptr;
+    if (need > 0 && noalloc_scratch(&ws)) return -1;
+    return selective_scan(a, ws, need > 0 ? kNoAllocScratchBytes : 0, st);
 }
 
 unsigned device_error_flags(bool clear) {

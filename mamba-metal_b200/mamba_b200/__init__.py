@@ -95,6 +95,7 @@ _PROTOTYPES = {
                                    ctypes.POINTER(c_i64), ctypes.POINTER(c_i64)]),
     "mamba_selective_scan_workspace": (c_size, [ctypes.POINTER(MambaScanArgs)]),
     "mamba_selective_scan": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_size, c_void_p]),
+    "mamba_selective_scan_noalloc": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p]),
     "mamba_scan_summary": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_void_p, c_void_p,
                                    c_size, c_void_p]),
     "mamba_scan_compose_prefix": (c_int, [c_void_p, c_int, c_int, c_i64, c_void_p, c_void_p,
