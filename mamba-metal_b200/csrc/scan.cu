@@ -15,11 +15,12 @@
 // channels of one batch row and one time chunk.
 //
 // Staging.  When x, delta and z are channel-contiguous with 16-byte aligned
-// rows (the layout of the model's activations), a 6-stage TMA pipeline
-// brings [8 timesteps x 128 channels] tiles of each into shared memory
-// (cp.async.bulk.tensor, completion on an mbarrier), so the compute threads
-// issue no global loads for them; B and C (shared by every channel) are
-// prefetched one tile ahead through registers into an FP32 double buffer.
+// rows (the layout of the model's activations), a 3-stage TMA pipeline
+// brings [16 timesteps x 128 channels] tiles of each, and the [16 x N] tiles
+// of B and C, into shared memory (cp.async.bulk.tensor, completion on an
+// mbarrier), so the compute threads issue no global loads; each B/C tile is
+// converted once per CTA into an FP32 double buffer read with broadcast
+// loads.  B/C layouts TMA cannot describe are prefetched through registers.
 // Any other layout goes through the generic kernel, which stages tiles with
 // cooperative loads along whichever axis is contiguous.
 //
@@ -51,15 +52,10 @@ namespace {
 
 constexpr int kScanCH = 128;    // channels (= threads) per CTA
 constexpr int kGenTT = 32;      // generic kernel: timesteps per tile
-#ifndef MAMBA_SCAN_TT
-#define MAMBA_SCAN_TT 8
-#endif
-#ifndef MAMBA_SCAN_STAGES
-#define MAMBA_SCAN_STAGES 6
-#endif
-constexpr int kTmaTT = MAMBA_SCAN_TT;          // TMA kernel: timesteps per tile
-constexpr int kTmaStages = MAMBA_SCAN_STAGES;  // TMA pipeline depth
-constexpr int kSubTT = 8;                      // generic kernel: timesteps per register batch
+constexpr int kTmaTT = 16;      // TMA kernel: timesteps per tile
+constexpr int kTmaStages = 3;   // TMA pipeline depth (48 timesteps in flight)
+constexpr int kTmaMinCtas = 5;  // resident CTAs per SM the TMA kernel is built for
+constexpr int kSubTT = 8;       // timesteps per register batch inside a tile
 constexpr int kChunkAlign = 32; // chunk lengths are multiples of both tile sizes
 
 enum ScanMode { kModeOutput = 0, kModeSummary = 1 };
@@ -280,39 +276,68 @@ __global__ void __launch_bounds__(CH) scan_generic_kernel(const ScanKParams p) {
 }
 
 // ---- TMA-pipelined kernel (channel-contiguous, 16-byte aligned rows) ---------
-template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt>
+template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt, typename Tbc>
 struct TmaLayout {
-    static constexpr int kXB = TT * CH * (int)sizeof(Tx);   // x or z tile bytes
-    static constexpr int kDB = TT * CH * (int)sizeof(Tdt);  // delta tile bytes
-    static constexpr int kStage = 2 * kXB + kDB;            // x | delta | z
-    static constexpr int kBC = 2 * TT * 2 * NS * 4;         // double-buffered FP32 B/C
+    static constexpr int align128(int v) { return (v + 127) / 128 * 128; }
+    static constexpr int kXB = TT * CH * (int)sizeof(Tx);            // x or z tile
+    static constexpr int kDB = TT * CH * (int)sizeof(Tdt);           // delta tile
+    static constexpr int kBCB = align128(TT * NS * (int)sizeof(Tbc)); // raw B or C tile
+    static constexpr int kOffD = kXB, kOffZ = kXB + kDB, kOffB = 2 * kXB + kDB, kOffC = kOffB + kBCB;
+    static constexpr int kStage = kOffC + kBCB;                       // x | delta | z | B | C
+    static constexpr int kBC = 2 * TT * 2 * NS * 4;                   // double-buffered FP32 B/C
     static constexpr int kBytes = ST * kStage + kBC + ST * 8;
     static_assert(kXB % 128 == 0 && kDB % 128 == 0, "TMA tiles must stay 128-byte aligned");
 };
 
-template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt, typename Tbc, int MODE, int EMUL>
-__global__ void __launch_bounds__(CH)
+// Convert the raw B and C tiles of one stage into the FP32 [TT][2*NS] layout
+// the recurrence reads (zero beyond N and beyond the chunk end).
+template <int NS, int CH, int TT, typename Tbc, bool SUMMARY>
+__device__ __forceinline__ void convert_bc(const Tbc *__restrict__ rawB, const Tbc *__restrict__ rawC,
+                                           float *__restrict__ dst, int N, int t0, int t_end) {
+    constexpr int kElems = TT * 2 * NS;
+#pragma unroll
+    for (int k = 0; k < (kElems + CH - 1) / CH; ++k) {
+        const int e = threadIdx.x + k * CH;
+        if (e < kElems) {
+            const int tt = e / (2 * NS), j = e % (2 * NS);
+            const int n = j < NS ? j : j - NS;
+            float v = 0.f;
+            if (n < N && t0 + tt < t_end && (j < NS || !SUMMARY))
+                v = cvt_f32(j < NS ? rawB[tt * N + n] : rawC[tt * N + n]);
+            dst[e] = v;
+        }
+    }
+}
+
+// BCTMA: B and C also arrive by TMA (when their layout allows it);
+// otherwise each thread prefetches its share through registers.
+template <int NS, int CH, int TT, int ST, typename Tx, typename Tdt, typename Tbc, int MODE, bool BCTMA>
+__global__ void __launch_bounds__(CH, kTmaMinCtas)
     scan_tma_kernel(const ScanKParams p, const __grid_constant__ CUtensorMap tmx,
-                    const __grid_constant__ CUtensorMap tmdt, const __grid_constant__ CUtensorMap tmz) {
+                    const __grid_constant__ CUtensorMap tmdt, const __grid_constant__ CUtensorMap tmz,
+                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC) {
     constexpr bool PRECISE = std::is_same<Tx, float>::value;
     constexpr bool SUMMARY = MODE == kModeSummary;
-    using Lay = TmaLayout<NS, CH, TT, ST, Tx, Tdt>;
+    using Lay = TmaLayout<NS, CH, TT, ST, Tx, Tdt, Tbc>;
     extern __shared__ __align__(128) unsigned char smem[];
-    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);            // [2][TT][2*NS]
+    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);                    // [2][TT][2*NS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ST * Lay::kStage + Lay::kBC);  // [ST]
 
     const int tid = threadIdx.x;
     const int b = blockIdx.z, chunk = blockIdx.y;
     const int d0 = blockIdx.x * CH, d = d0 + tid;
     const bool dvalid = d < p.D;
+    const int N = p.N;
     const int t_begin = chunk * p.chunk_len;
     const int t_end = min(p.L, t_begin + p.chunk_len);
     const int ntiles = t_end > t_begin ? (t_end - t_begin + TT - 1) / TT : 0;
     const bool has_z = !SUMMARY && p.z != nullptr;
-    const uint32_t tx_bytes = Lay::kXB + Lay::kDB + (has_z ? Lay::kXB : 0);
+    const uint32_t bc_box = (uint32_t)(N * TT * (int)sizeof(Tbc));
+    const uint32_t tx_bytes = Lay::kXB + Lay::kDB + (has_z ? Lay::kXB : 0) +
+                              (BCTMA ? bc_box * (SUMMARY ? 1u : 2u) : 0u);
 
     float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
-    const bool small = load_channel_consts<NS, PRECISE>(p.A, d, p.N, dvalid, Ac, kI);
+    const bool small = load_channel_consts<NS, PRECISE>(p.A, d, N, dvalid, Ac, kI);
     if (dvalid && !SUMMARY) load_initial_state<NS>(p, b, chunk, d, h, P);
     else load_initial_state<NS>(ScanKParams{}, 0, 0, 0, h, P);
     const bool has_bias = p.dt_bias != nullptr;
@@ -323,6 +348,10 @@ __global__ void __launch_bounds__(CH)
         prefetch_tensormap(&tmx);
         prefetch_tensormap(&tmdt);
         if (has_z) prefetch_tensormap(&tmz);
+        if (BCTMA) {
+            prefetch_tensormap(&tmB);
+            if (!SUMMARY) prefetch_tensormap(&tmC);
+        }
         for (int s = 0; s < ST; ++s) mbar_init(&bars[s], 1);
         fence_mbar_init();
     }
@@ -333,41 +362,64 @@ __global__ void __launch_bounds__(CH)
         const int t = t_begin + tile * TT;
         mbar_arrive_expect_tx(&bars[s], tx_bytes);
         tma_load_3d(stg, &tmx, &bars[s], d0, t, b);
-        tma_load_3d(stg + Lay::kXB, &tmdt, &bars[s], d0, t, b);
-        if (has_z) tma_load_3d(stg + Lay::kXB + Lay::kDB, &tmz, &bars[s], d0, t, b);
+        tma_load_3d(stg + Lay::kOffD, &tmdt, &bars[s], d0, t, b);
+        if (has_z) tma_load_3d(stg + Lay::kOffZ, &tmz, &bars[s], d0, t, b);
+        if (BCTMA) {
+            tma_load_3d(stg + Lay::kOffB, &tmB, &bars[s], 0, t, b);
+            if (!SUMMARY) tma_load_3d(stg + Lay::kOffC, &tmC, &bars[s], 0, t, b);
+        }
+    };
+    auto stage_bc = [&](int s, int t0, float *dst) {
+        const unsigned char *stg = smem + s * Lay::kStage;
+        convert_bc<NS, CH, TT, Tbc, SUMMARY>(reinterpret_cast<const Tbc *>(stg + Lay::kOffB),
+                                             reinterpret_cast<const Tbc *>(stg + Lay::kOffC), dst, N, t0, t_end);
     };
     if (tid == 0)
         for (int s = 0; s < min(ST, ntiles); ++s) issue(s, s);
 
     BCTile<NS, CH, TT, Tbc, SUMMARY> bc;
+    bool ok0 = true;
     if (ntiles > 0) {
-        bc.load(p, b, t_begin, t_end);
-        bc.store(bcf);
+        if (BCTMA) {
+            ok0 = mbar_wait_bounded(&bars[0], 0u);
+            if (ok0) stage_bc(0, t_begin, bcf);
+        } else {
+            bc.load(p, b, t_begin, t_end);
+            bc.store(bcf);
+        }
     }
-    __syncthreads();
-
     int i = 0;
-    bool aborted = false;
-    for (; i < ntiles; ++i) {
+    bool aborted = __syncthreads_or(!ok0);
+    for (; !aborted && i < ntiles; ++i) {
         const int s = i % ST;
         const int t0 = t_begin + i * TT;
         const int nt = min(TT, t_end - t0);
-        if (i + 1 < ntiles) bc.load(p, b, t0 + TT, t_end);
-        const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((i / ST) & 1));
+        if (!BCTMA && i + 1 < ntiles) bc.load(p, b, t0 + TT, t_end);
+        bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((i / ST) & 1));
         if (ok && dvalid) {
             const unsigned char *stg = smem + s * Lay::kStage;
             const Tx *sX = reinterpret_cast<const Tx *>(stg);
-            const Tdt *sDt = reinterpret_cast<const Tdt *>(stg + Lay::kXB);
-            const Tx *sZ = reinterpret_cast<const Tx *>(stg + Lay::kXB + Lay::kDB);
+            const Tdt *sDt = reinterpret_cast<const Tdt *>(stg + Lay::kOffD);
+            const Tx *sZ = reinterpret_cast<const Tx *>(stg + Lay::kOffZ);
             const float *sBC = bcf + (i & 1) * TT * 2 * NS;
             if (any_small)
-                run_tile<NS, CH, TT, SUMMARY, PRECISE, true, EMUL>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
-                                                              dskip, has_z, h, Ac, kI, P);
+                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, true, 0>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                                                                   bias, dskip, has_z, h, Ac, kI, P);
             else
-                run_tile<NS, CH, TT, SUMMARY, PRECISE, false, EMUL>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
-                                                               bias, dskip, has_z, h, Ac, kI, P);
+                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, false, 0>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                                                                    bias, dskip, has_z, h, Ac, kI, P);
         }
-        if (i + 1 < ntiles) bc.store(bcf + ((i + 1) & 1) * TT * 2 * NS);
+        if (i + 1 < ntiles) {
+            float *next = bcf + ((i + 1) & 1) * TT * 2 * NS;
+            if (BCTMA) {
+                const int s1 = (i + 1) % ST;
+                const bool ok1 = mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1));
+                if (ok1) stage_bc(s1, t0 + TT, next);
+                ok = ok && ok1;
+            } else {
+                bc.store(next);
+            }
+        }
         // One barrier per tile: the stage and the B/C buffer are free again,
         // and a timed-out wait anywhere in the CTA aborts all of it.
         if (__syncthreads_or(!ok)) {
@@ -440,22 +492,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 3-D map over a [batch, L, D] tensor with channel stride 1; box
-// [1, TT, CH].  False when the layout does not meet the TMA rules (16-byte
-// aligned base and strides), in which case the generic kernel is used.
-bool encode_map(CUtensorMap *m, const void *ptr, int dtype, int D, int L, int B, const int64_t *st) {
+// 3-D map over a [batch, L, dim0] tensor with stride 1 along dim0; box
+// [1, TT, box0].  False when the layout does not meet the TMA rules
+// (16-byte aligned base, 16-byte multiple strides and box rows), in which
+// case another staging path is used.
+bool encode_map(CUtensorMap *m, const void *ptr, int dtype, int dim0, int L, int B, const int64_t *st, int box0) {
     auto fn = tensor_map_encoder();
     if (!fn || !ptr || st[2] != 1) return false;
     const int64_t es = dtype == MAMBA_F16 ? 2 : 4;
-    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 || (box0 * es) % 16) return false;
     const int64_t row = st[1] * es;
     int64_t bat = st[0] * es;
-    if (row <= 0 || row % 16 || row < D * es) return false;
+    if (row <= 0 || row % 16 || row < dim0 * es) return false;
     if (B == 1) bat = row * std::max(L, 1);
     if (bat <= 0 || bat % 16) return false;
-    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)B};
+    cuuint64_t dims[3] = {(cuuint64_t)dim0, (cuuint64_t)L, (cuuint64_t)B};
     cuuint64_t strides[2] = {(cuuint64_t)row, (cuuint64_t)bat};
-    cuuint32_t box[3] = {(cuuint32_t)kScanCH, (cuuint32_t)kTmaTT, 1};
+    cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)kTmaTT, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = fn(m, dtype == MAMBA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                           3, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -464,16 +517,15 @@ bool encode_map(CUtensorMap *m, const void *ptr, int dtype, int D, int L, int B,
     return r == CUDA_SUCCESS;
 }
 
-template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE, int EMUL>
-int launch_tma(const ScanKParams &kp, const CUtensorMap &mx, const CUtensorMap &mdt, const CUtensorMap &mz,
-               cudaStream_t st) {
+template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE, bool BCTMA>
+int launch_tma(const ScanKParams &kp, const CUtensorMap *maps, cudaStream_t st) {
     constexpr int CH = kScanCH, TT = kTmaTT, ST = kTmaStages;
-    auto kern = scan_tma_kernel<NS, CH, TT, ST, Tx, Tdt, Tbc, MODE, EMUL>;
-    const int smem = TmaLayout<NS, CH, TT, ST, Tx, Tdt>::kBytes;
+    auto kern = scan_tma_kernel<NS, CH, TT, ST, Tx, Tdt, Tbc, MODE, BCTMA>;
+    const int smem = TmaLayout<NS, CH, TT, ST, Tx, Tdt, Tbc>::kBytes;
     MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     dim3 grid(ceil_div(kp.D, CH), kp.nchunks, kp.batch);
-    kern<<<grid, CH, smem, st>>>(kp, mx, mdt, mz);
+    kern<<<grid, CH, smem, st>>>(kp, maps[0], maps[1], maps[2], maps[3], maps[4]);
     return launch_status("selective_scan (TMA) kernel");
 }
 
@@ -489,34 +541,41 @@ int launch_generic(const ScanKParams &kp, cudaStream_t st) {
 }
 
 template <int NS, typename Tx, typename Tdt, typename Tbc, int MODE>
-int launch_scan_ns(const ScanKParams &kp, int xd, int dd, cudaStream_t st) {
-    CUtensorMap mx, mdt, mz;
+int launch_scan_ns(const ScanKParams &kp, int xd, int dd, int bd, cudaStream_t st) {
+    CUtensorMap maps[5];  // x, delta, z, B, C
     const bool want_z = MODE == kModeOutput && kp.z != nullptr;
-    const bool tma = kp.L > 0 && encode_map(&mx, kp.x, xd, kp.D, kp.L, kp.batch, kp.sx) &&
-                     encode_map(&mdt, kp.delta, dd, kp.D, kp.L, kp.batch, kp.sdt) &&
-                     (!want_z || encode_map(&mz, kp.z, xd, kp.D, kp.L, kp.batch, kp.sz));
+    const bool tma = kp.L > 0 && encode_map(&maps[0], kp.x, xd, kp.D, kp.L, kp.batch, kp.sx, kScanCH) &&
+                     encode_map(&maps[1], kp.delta, dd, kp.D, kp.L, kp.batch, kp.sdt, kScanCH) &&
+                     (!want_z || encode_map(&maps[2], kp.z, xd, kp.D, kp.L, kp.batch, kp.sz, kScanCH));
     if (!tma) return launch_generic<NS, Tx, Tdt, Tbc, MODE>(kp, st);
-    if (!want_z) mz = mx;  // unused by the kernel
-    return launch_tma<NS, Tx, Tdt, Tbc, MODE, 0>(kp, mx, mdt, mz, st);
+    if (!want_z) maps[2] = maps[0];  // unused by the kernel
+    const bool bc_tma = kp.N == NS && encode_map(&maps[3], kp.B, bd, kp.N, kp.L, kp.batch, kp.sB, kp.N) &&
+                        (MODE == kModeSummary || encode_map(&maps[4], kp.C, bd, kp.N, kp.L, kp.batch, kp.sC, kp.N));
+    if (bc_tma) {
+        if (MODE == kModeSummary) maps[4] = maps[3];  // unused by the kernel
+        return launch_tma<NS, Tx, Tdt, Tbc, MODE, true>(kp, maps, st);
+    }
+    maps[3] = maps[4] = maps[0];  // unused by the kernel
+    return launch_tma<NS, Tx, Tdt, Tbc, MODE, false>(kp, maps, st);
 }
 
 template <typename Tx, typename Tdt, typename Tbc, int MODE>
-int launch_scan_n(const ScanKParams &kp, int xd, int dd, cudaStream_t st) {
-    if (kp.N <= 4) return launch_scan_ns<4, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
-    if (kp.N <= 8) return launch_scan_ns<8, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
-    return launch_scan_ns<16, Tx, Tdt, Tbc, MODE>(kp, xd, dd, st);
+int launch_scan_n(const ScanKParams &kp, int xd, int dd, int bd, cudaStream_t st) {
+    if (kp.N <= 4) return launch_scan_ns<4, Tx, Tdt, Tbc, MODE>(kp, xd, dd, bd, st);
+    if (kp.N <= 8) return launch_scan_ns<8, Tx, Tdt, Tbc, MODE>(kp, xd, dd, bd, st);
+    return launch_scan_ns<16, Tx, Tdt, Tbc, MODE>(kp, xd, dd, bd, st);
 }
 
 template <int MODE>
 int launch_scan_dtypes(const ScanKParams &kp, int xd, int dd, int bd, cudaStream_t st) {
     if (xd == MAMBA_F32 && dd == MAMBA_F32 && bd == MAMBA_F32)
-        return launch_scan_n<float, float, float, MODE>(kp, xd, dd, st);
+        return launch_scan_n<float, float, float, MODE>(kp, xd, dd, bd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F16 && bd == MAMBA_F16)
-        return launch_scan_n<__half, __half, __half, MODE>(kp, xd, dd, st);
+        return launch_scan_n<__half, __half, __half, MODE>(kp, xd, dd, bd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F16)
-        return launch_scan_n<__half, float, __half, MODE>(kp, xd, dd, st);
+        return launch_scan_n<__half, float, __half, MODE>(kp, xd, dd, bd, st);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F32)
-        return launch_scan_n<__half, float, float, MODE>(kp, xd, dd, st);
+        return launch_scan_n<__half, float, float, MODE>(kp, xd, dd, bd, st);
     set_error("selective_scan: unsupported dtype combination (x, delta, B/C)");
     return -1;
 }
