@@ -11,6 +11,12 @@ Workloads (synthetic inputs, random-init weights; no datasets involved):
                    collective); value = tokens/s of the whole job.  The scan
                    kernel's HBM GB/s is measured live with CUDA events over
                    the timed region and reported in `roofline`.
+  block            one Mamba block forward, d_model 768, d_inner 1536, batch 8,
+                   L 2048, FP16; value = tokens/s (batch-sharded at N > 1).
+  decode           incremental decode through mamba_step on a 64-layer stack,
+                   d_model 2560, d_inner 5120, dt_rank 160, batch 256, 1024
+                   sequential single-token steps from zero state (CUDA-graph
+                   replayed); value = tokens/s, plus per-step latency.
   scan             standalone long selective scan, batch 1, d_inner 2048,
                    d_state 16, L 131072; x, B, C, z FP16, delta FP32; the
                    sequence is split across the N ranks with one all-gather
@@ -39,6 +45,8 @@ for _p in (ROOT, os.path.join(ROOT, "mamba-metal_b200")):
 import numpy as np  # noqa: E402
 
 STACK = dict(d_model=2048, d_state=16, d_conv=4, expand=2, n_layer=48, batch=64, seqlen=4096)
+BLOCK = dict(d_model=768, d_state=16, d_conv=4, expand=2, n_layer=1, batch=8, seqlen=2048)
+DECODE = dict(d_model=2560, d_state=16, d_conv=4, expand=2, n_layer=64, batch=256, decode_steps=1024)
 SCAN = dict(batch=1, d_inner=2048, d_state=16, seqlen=131072)
 METRIC = "selective-scan HBM GB/s (% peak) and block fwd tokens/s at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
@@ -245,19 +253,22 @@ def stack_config_dict(world):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_stack(args, world, rank, local):
+def run_stack(args, world, rank, local, C=STACK):
     import torch
     import mamba_b200 as mb
-    n_layer = args.layers or STACK["n_layer"]
-    gb = args.batch or STACK["batch"]
-    L = args.seqlen or STACK["seqlen"]
+    n_layer = args.layers or C["n_layer"]
+    gb = args.batch or C["batch"]
+    L = args.seqlen or C["seqlen"]
     if gb % world:
         raise SystemExit("global batch %d not divisible by %d ranks" % (gb, world))
     b = gb // world
-    M, D, N = STACK["d_model"], STACK["d_model"] * STACK["expand"], STACK["d_state"]
-    model = mb.Model(M, N, STACK["d_conv"], STACK["expand"], n_layer, mb.F16)
+    M, D, N = C["d_model"], C["d_model"] * C["expand"], C["d_state"]
+    model = mb.Model(M, N, C["d_conv"], C["expand"], n_layer, mb.F16)
     model.init_random(1234)
-    stream = torch.cuda.current_stream()
+    # All work of the timed region on one explicit stream: the model's calls
+    # (set_stream) and the CUDA events that time them.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     g = torch.Generator(device="cuda")
     g.manual_seed(1000 + rank)
@@ -317,14 +328,22 @@ def run_stack(args, world, rank, local):
                "api": "mamba_forward (host FP32, pinned)"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and C is STACK:
         tps, sample = cpu_stack_tokens_per_s(budget_s=args.cpu_budget, use_reference_scan=False)
         cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                "sample": sample}
 
     if rank == 0:
-        cfgd = stack_config_dict(world)
-        if n_layer != STACK["n_layer"] or gb != STACK["batch"] or L != STACK["seqlen"]:
+        if C is STACK:
+            cfgd = stack_config_dict(world)
+        else:
+            cfgd = {"workload": "mamba block forward: %d layer, d_model %d, d_inner %d, d_state %d, d_conv %d, "
+                                "dt_rank %d, batch %d, L %d" % (C["n_layer"], M, D, N, C["d_conv"], (M + 15) // 16,
+                                                                C["batch"], C["seqlen"]),
+                    "global_batch": C["batch"], "seq_len": C["seqlen"],
+                    "parallelism": "batch-sharded dp%d (no collective)" % world,
+                    "l2": "activations exceed L2 between steps only partly; reported as measured"}
+        if n_layer != C["n_layer"] or gb != C["batch"] or L != C["seqlen"]:
             cfgd["reduced"] = {"n_layer": n_layer, "batch": gb, "seqlen": L}
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
@@ -343,6 +362,76 @@ def run_stack(args, world, rank, local):
         print(json.dumps(line))
 
 
+def run_decode(args, world, rank, local):
+    import torch
+    import mamba_b200 as mb
+    C = DECODE
+    n_layer = args.layers or C["n_layer"]
+    gb = args.batch or C["batch"]
+    K = args.decode_steps or C["decode_steps"]
+    if gb % world:
+        raise SystemExit("global batch %d not divisible by %d ranks" % (gb, world))
+    b = gb // world
+    M, D, N = C["d_model"], C["d_model"] * C["expand"], C["d_state"]
+    model = mb.Model(M, N, C["d_conv"], C["expand"], n_layer, mb.F16)
+    model.init_random(4321)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    model.set_stream(stream.cuda_stream)
+    st = model.create_state(b)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(500 + rank)
+    toks = torch.randn((K, b, M), device="cuda", dtype=torch.float32, generator=g)
+    cur = torch.empty((b, M), device="cuda")
+    out = torch.empty_like(cur)
+
+    def step(i):
+        cur.copy_(toks[i % K])
+        st.step_device(cur.data_ptr(), out.data_ptr(), stream.cuda_stream)
+
+    for i in range(args.warmup):
+        step(i)
+    # per-operation times from a few profiled (graph-free) steps
+    model.profile(True)
+    for i in range(2):
+        step(i)
+    prof = model.profile_read()
+    model.profile(False)
+    st.reset()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(world)
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    peak, peak_src = peaks()
+    ssm_ms = prof["scan"][0] / max(prof["scan"][1], 1)
+    ssm_bytes = b * D * N * 4 * 2 + b * D * 2 * 4 + b * 2 * N * 2 + D * N * 4 + 2 * D * 4
+    if rank == 0:
+        line = {"metric": METRIC, "value": gb * K / (t_ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+                "steps": K, "warmup": args.warmup, "ms_per_step": t_ms / K, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "f16 activations/weights, f32 conv/ssm state", "data": "synthetic",
+                "config": {"workload": "decode: %d layers, d_model %d, d_inner %d, d_state %d, dt_rank %d, "
+                                       "batch %d, %d steps from zero state" % (n_layer, M, D, N, (M + 15) // 16,
+                                                                               gb, K),
+                           "parallelism": "batch-sharded dp%d (weights replicated)" % world},
+                "roofline": {"kernel": "ssm_step (decode state update)", "bound": "hbm",
+                             "achieved": ssm_bytes / (ssm_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": ssm_bytes / (ssm_ms / 1e3) / 1e9 / peak, "peak_source": peak_src,
+                             "algorithmic_bytes_per_launch": ssm_bytes, "avg_launch_ms": ssm_ms,
+                             "traffic": None},
+                "op_ms_per_layer": {k: round(v[0] / max(v[1], 1), 4) for k, v in prof.items()},
+                "gpu_launches": 2 * n_layer * K, "clocks": clk}
+        print(json.dumps(line))
+
+
 def run_scan(args, world, rank, local):
     import torch
     import mamba_b200 as mb
@@ -350,6 +439,8 @@ def run_scan(args, world, rank, local):
     Lg = args.seqlen or SCAN["seqlen"]
     if Lg % world:
         raise SystemExit("seqlen not divisible by ranks")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     L = Lg // world
     D, N = SCAN["d_inner"], SCAN["d_state"]
     g = torch.Generator(device="cuda")
@@ -373,10 +464,10 @@ def run_scan(args, world, rank, local):
     clocks = ClockSampler(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(stream)
     for _ in range(args.steps):
         step()
-    e1.record()
+    e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier(world)
@@ -403,7 +494,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack", "scan"])
+    ap.add_argument("--workload", default="stack", choices=["stack", "block", "decode", "scan"])
+    ap.add_argument("--decode-steps", type=int, default=0, help="decode workload: steps timed")
     ap.add_argument("--layers", type=int, default=0, help="override n_layer (reduced runs)")
     ap.add_argument("--batch", type=int, default=0, help="override global batch")
     ap.add_argument("--seqlen", type=int, default=0, help="override L")
@@ -424,6 +516,10 @@ def main():
     try:
         if args.workload == "scan":
             run_scan(args, world, rank, local)
+        elif args.workload == "decode":
+            run_decode(args, world, rank, local)
+        elif args.workload == "block":
+            run_stack(args, world, rank, local, C=BLOCK)
         else:
             run_stack(args, world, rank, local)
     finally:

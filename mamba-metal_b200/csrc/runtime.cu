@@ -19,6 +19,7 @@
 #include <cublas_v2.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -161,6 +162,24 @@ struct OpScope {
     }
 };
 
+// One decode step of every layer captured as a CUDA graph, replayed while
+// the state buffers, token/output pointers, arena and stream stay the same.
+struct StepGraph {
+    const float *conv = nullptr, *ssm = nullptr;
+    int batch = -1;
+    const float *in = nullptr;
+    float *out = nullptr;
+    cudaStream_t st = nullptr;
+    const void *arena = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    void reset() {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        batch = -1;
+    }
+    ~StepGraph() { reset(); }
+};
+
 }  // namespace
 
 struct Model {
@@ -183,11 +202,15 @@ struct Model {
     // caller-provided stream (mamba_set_stream) and tracing
     cudaStream_t user_stream = nullptr;
     Profiler prof;
+    // decode graph (MAMBA_STEP_GRAPH=0 disables)
+    StepGraph step_graph;
+    bool use_graphs = true;
 
     cudaStream_t cur_stream() const { return user_stream ? user_stream : stream; }
 
     ~Model() {
         if (stream) cudaStreamSynchronize(stream);
+        step_graph.reset();
         if (cublas) cublasDestroy(cublas);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -225,6 +248,7 @@ struct Model {
         MB_CHECK_ARG(prop.major == 10, std::string("mamba_create: device '") + prop.name +
                                            "' is not sm_100 (compute capability 10.x required)");
         MB_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        if (const char *g = std::getenv("MAMBA_STEP_GRAPH")) use_graphs = std::atoi(g) != 0;
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -475,17 +499,12 @@ static int ensure_step_arena(Model &m, int rows, StepArena &ar) {
     return 0;
 }
 
-static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *out, cudaStream_t st) {
-    MB_CHECK_ARG(tok && out, "step: null pointer");
-    MB_CHECK_ARG(s.dev == m.dev && s.n_layer == m.cfg.n_layer && s.D == m.D && s.N == m.N && s.K == m.K,
-                 "step: state does not belong to this model's configuration");
+// Enqueues one decode step of every layer on `st` (the arena is ready).
+static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *out, cudaStream_t st,
+                        const StepArena &ar) {
     const int Bt = s.batch;
-    if (Bt == 0) return 0;
-    if (!st) st = m.cur_stream();
     if (tok != out)
         MB_CUDA_TRY(cudaMemcpyAsync(out, tok, sizeof(float) * Bt * m.M, cudaMemcpyDeviceToDevice, st));
-    StepArena ar{};
-    if (ensure_step_arena(m, Bt, ar)) return -1;
     const size_t a = m.act_size();
     const int D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
     Profiler &pf = m.prof;
@@ -528,6 +547,53 @@ static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *o
             if (m.gemm(st, Bt, m.M, D, ar.y, D, w.w_out_t, out, m.M, MAMBA_F32, 1.f)) return -1;
         }
     }
+    return 0;
+}
+
+static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *out, cudaStream_t st) {
+    MB_CHECK_ARG(tok && out, "step: null pointer");
+    MB_CHECK_ARG(s.dev == m.dev && s.n_layer == m.cfg.n_layer && s.D == m.D && s.N == m.N && s.K == m.K,
+                 "step: state does not belong to this model's configuration");
+    const int Bt = s.batch;
+    if (Bt == 0) return 0;
+    if (!st) st = m.cur_stream();
+    StepArena ar{};
+    if (ensure_step_arena(m, Bt, ar)) return -1;  // any allocation happens before a capture
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    MB_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+    // Plain launches when graphs are off, while profiling (events per
+    // operation), or when the caller is capturing the stream itself.
+    if (!m.use_graphs || m.prof.on || cs != cudaStreamCaptureStatusNone) return step_enqueue(m, s, tok, out, st, ar);
+    StepGraph &g = m.step_graph;
+    const bool hit = g.exec && g.conv == s.conv && g.ssm == s.ssm && g.batch == Bt && g.in == tok && g.out == out &&
+                     g.st == st && g.arena == m.step_arena.ptr;
+    if (!hit) {
+        g.reset();
+        MB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        const int rc = step_enqueue(m, s, tok, out, st, ar);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc || e != cudaSuccess || !graph) {
+            if (graph) cudaGraphDestroy(graph);
+            if (!rc) set_error(std::string("step: graph capture failed: ") + cudaGetErrorString(e));
+            return -1;
+        }
+        const cudaError_t ei = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ei != cudaSuccess) {
+            g.exec = nullptr;
+            set_error(std::string("step: graph instantiation failed: ") + cudaGetErrorString(ei));
+            return -1;
+        }
+        g.conv = s.conv;
+        g.ssm = s.ssm;
+        g.batch = Bt;
+        g.in = tok;
+        g.out = out;
+        g.st = st;
+        g.arena = m.step_arena.ptr;
+    }
+    MB_CUDA_TRY(cudaGraphLaunch(g.exec, st));
     return 0;
 }
 
