@@ -165,10 +165,17 @@ class ClockSampler:
 def cpu_stack_tokens_per_s(budget_s, use_reference_scan, tokens=256, seed=0):
     """Times the CPU restatement of the stack workload's layer on one
     sequence of `tokens` tokens; per-token throughput of the full 48-layer
-    stack is extrapolated from the measured per-layer time."""
+    stack is extrapolated from the measured per-layer time.  Uses every host
+    thread (torchrun sets OMP_NUM_THREADS=1, so the BLAS pool is resized)."""
     import oracle  # noqa: F401  (CPU checker, only in this leg)
     from oracle import block_ref
     import mamba_b200 as mb
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(limits=os.cpu_count() or 1):
+        return _cpu_stack(budget_s, use_reference_scan, tokens, seed, oracle, block_ref, mb)
+
+
+def _cpu_stack(budget_s, use_reference_scan, tokens, seed, oracle, block_ref, mb):
     cfg = mb.MambaConfig(STACK["d_model"], STACK["d_state"], STACK["d_conv"], STACK["expand"],
                          STACK["n_layer"], mb.F16)
     rng = np.random.default_rng(seed)

@@ -82,11 +82,108 @@ __global__ void __launch_bounds__(128)
     y[(int64_t)b * yrs + d] = cvt_out<Tx>(scan_output<PRECISE>(s, dsk, xv, gate));
 }
 
+// FP16 fast path: four threads per channel, each owning NS/4 consecutive
+// states, so lane l of a warp reads and writes bytes [16 l, 16 l + 16) of a
+// contiguous 512-byte run (full coalescing) and four times as many threads
+// hide the state latency.  Each state sees exactly the per-state operations
+// of scan_step (fast mode); the four partial sums of C*h are combined with
+// two butterfly shuffles.
+template <int NS, typename Tx, typename Tdt, typename Tbc>
+__global__ void __launch_bounds__(128)
+    ssm_step_quad_kernel(const Tx *__restrict__ x, int64_t xrs, const Tdt *__restrict__ delta, int64_t drs,
+                         const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
+                         const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
+                         const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
+                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N) {
+    constexpr int S = NS / 4;  // states per thread
+    __shared__ __align__(16) float sBC[2 * NS];
+    const int b = blockIdx.y;
+    const int q = threadIdx.x & 3;
+    const int d = blockIdx.x * 32 + (threadIdx.x >> 2);
+    if (threadIdx.x < 2 * NS) {
+        const int j = threadIdx.x;
+        float v = 0.f;
+        if (j < NS) {
+            if (j < N) v = ld_f32(Bm + (int64_t)b * bcrs + j);
+        } else if (j - NS < N) {
+            v = ld_f32(Cm + (int64_t)b * bcrs + (j - NS));
+        }
+        sBC[j] = v;
+    }
+    __syncthreads();
+    // Lanes of channels past D stay to the end (every lane of the warp takes
+    // part in the shuffles below); only their memory accesses are skipped.
+    const bool valid = d < D;
+    const int dd = valid ? d : 0;
+    float ac[S], kI[S], h[S];
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        const int n = q * S + j;
+        const float a = (valid && n < N) ? A[(int64_t)dd * N + n] : 0.f;
+        ac[j] = a * kLog2e;
+        kI[j] = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
+        h[j] = 0.f;
+    }
+    float *hp = state + ((int64_t)b * D + dd) * N + q * S;
+    const bool vec = (NS == N) && (S == 4);
+    if (valid) {
+        if (vec) {
+            const float4 v = *reinterpret_cast<const float4 *>(hp);
+            h[0] = v.x;
+            h[S > 1 ? 1 : 0] = v.y;
+            h[S > 2 ? 2 : 0] = v.z;
+            h[S > 3 ? 3 : 0] = v.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < S; ++j) h[j] = q * S + j < N ? hp[j] : 0.f;
+        }
+    }
+    const float xv = valid ? ld_f32(x + (int64_t)b * xrs + dd) : 0.f;
+    float draw = valid ? ld_f32(delta + (int64_t)b * drs + dd) : 0.f;
+    if (dt_bias && valid) draw = __fadd_rn(draw, dt_bias[dd]);
+    const float dt = softplus_fast(draw);
+    float yp = 0.f;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        const int n = q * S + j;
+        const float a = ex2_approx(dt * ac[j]);
+        const float w = xv * sBC[n];
+        const float k = w * kI[j];
+        const float bb = kI[j] != 0.f ? fmaf(a, k, -k) : dt * w;
+        h[j] = fmaf(a, h[j], bb);
+        yp = fmaf(sBC[NS + n], h[j], yp);
+    }
+    yp += __shfl_xor_sync(0xffffffffu, yp, 1);
+    yp += __shfl_xor_sync(0xffffffffu, yp, 2);
+    if (!valid) return;
+    if (vec) {
+        *reinterpret_cast<float4 *>(hp) = make_float4(h[0], h[S > 1 ? 1 : 0], h[S > 2 ? 2 : 0], h[S > 3 ? 3 : 0]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < S; ++j)
+            if (q * S + j < N) hp[j] = h[j];
+    }
+    if (q == 0) {
+        const float dsk = Dskip ? Dskip[d] : 0.f;
+        const float gate = z ? silu_fast(ld_f32(z + (int64_t)b * zrs + d)) : 1.f;
+        y[(int64_t)b * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv, yp) * gate);
+    }
+}
+
 template <int NS, typename Tx, typename Tdt, typename Tbc>
 int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
                 const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
                 const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
                 int N, cudaStream_t st) {
+    if (!std::is_same<Tx, float>::value) {
+        // Four threads per channel, 32 channels per CTA.
+        dim3 grid(ceil_div(D, 32), batch);
+        ssm_step_quad_kernel<NS, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
+            static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
+            static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
+            static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, D, N);
+        return launch_status("ssm_step kernel");
+    }
     dim3 grid(ceil_div(D, 128), batch);
     ssm_step_kernel<NS, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
         static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,

@@ -60,10 +60,14 @@ def test_conv_step_sequence(cuda, dtype):
     assert np.array_equal(st.cpu().numpy(), st_ref)
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
-def test_ssm_step_sequence(cuda, dtype):
-    """T decode updates equal the oracle step (and so the scan)."""
-    bsz, L, D, N = 5, 12, 160, 16
+@pytest.mark.parametrize("dtype,D,N", [(torch.float32, 160, 16), (torch.float16, 160, 16),
+                                       (torch.float16, 100, 16), (torch.float16, 70, 8),
+                                       (torch.float16, 33, 5)])
+def test_ssm_step_sequence(cuda, dtype, D, N):
+    """T decode updates equal the oracle step (and so the scan); FP16 runs
+    the four-threads-per-channel kernel, including channel counts that leave
+    part of a warp without a channel."""
+    bsz, L = 5, 12
     x, dr, B, C, z, A, Dk = scan_inputs(13, bsz, L, D, N)
     bias = np.random.default_rng(0).normal(0, 0.5, D).astype(np.float32)
     if dtype == torch.float16:
@@ -80,6 +84,22 @@ def test_ssm_step_sequence(cuda, dtype):
         torch.cuda.synchronize()
         assert err(y, yr) < (TOL32 if dtype == torch.float32 else TOL16)
     assert err(st, st_ref) < TOL32
+
+
+def test_fp16_decode_states_match_scan_bitwise(cuda):
+    """The FP16 decode kernel applies the scan's per-state operations, so T
+    steps leave exactly the scan's final state."""
+    bsz, L, D, N = 3, 30, 256, 16
+    x, dr, B, C, z, A, Dk = scan_inputs(15, bsz, L, D, N)
+    h16 = lambda a: dev(a, torch.float16)  # noqa: E731
+    tx, tdr, tB, tC, tz = h16(x), h16(dr), h16(B), h16(C), h16(z)
+    tA, tD = dev(A), dev(Dk)
+    y_scan, h_scan = mb.selective_scan(tx, tdr, tA, tB, tC, D=tD, z=tz, return_final_state=True)
+    st = torch.zeros((bsz, D, N), device="cuda")
+    ys = [mb.ssm_step(tx[:, t], tdr[:, t], tA, tB[:, t], tC[:, t], st, D=tD, z=tz[:, t]) for t in range(L)]
+    torch.cuda.synchronize()
+    assert torch.equal(st, h_scan)
+    assert err(torch.stack(ys, 1), y_scan.float().cpu().numpy()) < 2e-3
 
 
 def test_ssm_step_matches_scan_final_state(cuda):
