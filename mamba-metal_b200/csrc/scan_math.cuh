@@ -9,10 +9,9 @@
 //    and rounded once to FP32, i.e. correctly rounded like the libm calls the
 //    oracle makes.  The zero-order hold's (a - 1) is ill-conditioned when
 //    dt*A is small, so matching the oracle's rounding matters here.
-//  * fast (FP16 inputs, 2e-3 budget): single-instruction ex2.approx, a
-//    polynomial exp2 on the FMA pipe for the first EMUL states (to balance
-//    the special-function and FMA pipes), short softplus/SiLU forms, and
-//    packed f32x2 arithmetic (two states per instruction).
+//  * fast (FP16 inputs, 2e-3 budget): single-instruction ex2.approx, short
+//    softplus/SiLU forms, and packed f32x2 arithmetic (two states per
+//    instruction).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -39,27 +38,6 @@ __device__ __forceinline__ float rcp_approx(float v) {
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
     return r;
-}
-
-// 2^x on the FMA pipe.  Range reduction 2^x = 2^j * 2^f with j = rint(x)
-// (the 1.5*2^23 rounding trick, which also leaves j in the low mantissa
-// bits) and f in [-1/2, 1/2]; 2^f from a degree-5 polynomial whose
-// coefficients interpolate 2^f at the six Chebyshev nodes of [-1/2, 1/2]
-// (max relative error 2.4e-7 in FP32 Horner form); 2^j is added directly to
-// the exponent field.  x is clamped to [-125, 127] so the result stays a
-// normal number.
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fminf(fmaxf(x, -125.f), 127.f);
-    const float t = x + 12582912.f;
-    const float j = t - 12582912.f;
-    const float f = x - j;
-    float p = 1.339086331e-03f;
-    p = fmaf(p, f, 9.676031768e-03f);
-    p = fmaf(p, f, 5.550356954e-02f);
-    p = fmaf(p, f, 2.402210683e-01f);
-    p = fmaf(p, f, 6.931471825e-01f);
-    p = fmaf(p, f, 1.000000119e+00f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // softplus(x) = max(x, 0) + log1p(e), e = exp(-|x|) in (0, 1], with one
@@ -114,8 +92,6 @@ __device__ __forceinline__ float scan_silu(float z) {
     return PRECISE ? silu_exact(z) : silu_fast(z);
 }
 
-__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
-
 // Per-channel constants of NS states packed in pairs: Ac = A (PRECISE) or
 // A*log2(e) (fast); kI = 1/A, or 0 where |A| <= 1e-6 (the dt*B branch of
 // selective_scan_cpu.cpp:28-30) and for padding states n >= N.
@@ -166,10 +142,17 @@ __device__ __forceinline__ float scan_step_exact(float xv, float dt, const float
     return yt;
 }
 
+// One state of the fast path: h' = a h + b with b = (a - 1)/A * w (w = B x)
+// or b = dt * w where |A| <= 1e-6 (kI == 0).  The zero-order-hold form is
+// evaluated as h + (a - 1)(h + w/A).
+__device__ __forceinline__ float state_update(float a, float w, float kI, float dt, float h) {
+    return kI != 0.f ? fmaf(a - 1.f, fmaf(w, kI, h), h) : fmaf(a, h, dt * w);
+}
+
 // One timestep for one channel.  bc points at the step's B[0..NS) and
 // C[0..NS) (FP32, 16-byte aligned).  Updates h (and P = prod a in summary
 // mode); returns sum_n C[n] * h[n] (output mode).
-template <int NS, bool SUMMARY, bool PRECISE, bool SMALLA, int EMUL>
+template <int NS, bool SUMMARY, bool PRECISE, bool SMALLA>
 __device__ __forceinline__ float scan_step(float xv, float dt, const float *__restrict__ bc, float2 *h,
                                            const float2 *Ac, const float2 *kI, float2 *P) {
     if (PRECISE) return scan_step_exact<NS, SUMMARY>(xv, dt, bc, h, Ac, kI, P);
@@ -191,19 +174,19 @@ __device__ __forceinline__ float scan_step(float xv, float dt, const float *__re
                 a.x = expf(dA.x);
                 a.y = expf(dA.y);
             } else {
-                a.x = (2 * p < EMUL) ? exp2_fma(dA.x) : ex2_approx(dA.x);
-                a.y = (2 * p + 1 < EMUL) ? exp2_fma(dA.y) : ex2_approx(dA.y);
+                a.x = ex2_approx(dA.x);
+                a.y = ex2_approx(dA.y);
             }
             const float2 w = __fmul2_rn(x2, Bp);
-            const float2 k = __fmul2_rn(w, kI[p]);
-            float2 bb;
             if (SMALLA) {
-                bb.x = (kI[p].x != 0.f) ? fmaf(a.x, k.x, -k.x) : dt * w.x;
-                bb.y = (kI[p].y != 0.f) ? fmaf(a.y, k.y, -k.y) : dt * w.y;
+                h[p].x = state_update(a.x, w.x, kI[p].x, dt, h[p].x);
+                h[p].y = state_update(a.y, w.y, kI[p].y, dt, h[p].y);
             } else {
-                bb = __ffma2_rn(a, k, neg2(k));
+                // h' = a h + (a - 1) k = h + (a - 1)(h + k): no negated operand,
+                // and the (a - 1) product stays well conditioned.
+                const float2 sk = __ffma2_rn(w, kI[p], h[p]);
+                h[p] = __ffma2_rn(__fadd2_rn(a, make_float2(-1.f, -1.f)), sk, h[p]);
             }
-            h[p] = __ffma2_rn(a, h[p], bb);
             if (SUMMARY) {
                 P[p] = __fmul2_rn(P[p], a);
             } else {

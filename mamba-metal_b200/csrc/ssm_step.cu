@@ -64,8 +64,8 @@ __global__ void __launch_bounds__(128)
     float draw = ld_f32(delta + (int64_t)b * drs + d);
     if (dt_bias) draw = __fadd_rn(draw, dt_bias[d]);
     const float dt = scan_softplus<PRECISE>(draw);
-    const float s = small ? scan_step<NS, false, PRECISE, true, 0>(xv, dt, sBC, h, Ac, kI, P)
-                          : scan_step<NS, false, PRECISE, false, 0>(xv, dt, sBC, h, Ac, kI, P);
+    const float s = small ? scan_step<NS, false, PRECISE, true>(xv, dt, sBC, h, Ac, kI, P)
+                          : scan_step<NS, false, PRECISE, false>(xv, dt, sBC, h, Ac, kI, P);
     if (vec) {
 #pragma unroll
         for (int i = 0; i < NS / 4; ++i)
@@ -147,10 +147,7 @@ __global__ void __launch_bounds__(128)
     for (int j = 0; j < S; ++j) {
         const int n = q * S + j;
         const float a = ex2_approx(dt * ac[j]);
-        const float w = xv * sBC[n];
-        const float k = w * kI[j];
-        const float bb = kI[j] != 0.f ? fmaf(a, k, -k) : dt * w;
-        h[j] = fmaf(a, h[j], bb);
+        h[j] = state_update(a, xv * sBC[n], kI[j], dt, h[j]);
         yp = fmaf(sBC[NS + n], h[j], yp);
     }
     yp += __shfl_xor_sync(0xffffffffu, yp, 1);
