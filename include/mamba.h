@@ -100,7 +100,8 @@ const char *mamba_last_error(void);
 /* Error flags raised by kernels on the current device since the last
  * clear (0 = none).  Bit 0: a shared-memory pipeline wait inside the
  * selective scan exceeded its 2-second bound, so that call stopped early and
- * its outputs are invalid.  Waits for the device; clear != 0 resets them. */
+ * its outputs are invalid.  Bit 1: the same for a wait inside
+ * mamba_gated_mlp_up.  Waits for the device; clear != 0 resets them. */
 unsigned mamba_device_status(int clear);
 
 /* dt_rank used for a config: ceil(d_model / 16). */
@@ -286,6 +287,35 @@ int mamba_ssm_step(const void *x, int64_t x_row_stride, const void *delta,
  * or NULL. */
 int mamba_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols, float eps,
                   int in_dtype, int out_dtype, void *stream);
+
+/* Exclusive propagation of per-tile affine carries: the job of
+ * propagate_tile_carries_f32 (prefix_scan.metal:19-40), with the pair layout
+ * that kernel documents and its indexing fixed.  carries FP32
+ * [num_tiles, width, 2], pair p of tile t at (t*width + p)*2 as (a, b);
+ * in place, tile t's pair becomes the composition of tiles 0..t-1
+ * ((1, 0) for tile 0), composed as (a2, b2) o (a1, b1) =
+ * (a2*a1, a2*b1 + b2) (prefix_scan.metal:12-14).  total FP32 [width, 2]
+ * (or NULL) receives the composition of all tiles.  8-byte aligned. */
+int mamba_propagate_tile_carries(float *carries, int num_tiles, int64_t width, float *total,
+                                 void *stream);
+
+/* SwiGLU gate (gated_silu_mul_f32/_f16, gated_mlp.metal:14-41):
+ * out[i] = silu(gate[i]) * up[i] for n elements of dtype (MAMBA_F32 or
+ * MAMBA_F16; FP16 computes in FP32 and rounds once). */
+int mamba_gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int dtype,
+                         void *stream);
+
+/* Fused SwiGLU up-projection on the tensor cores (no reference
+ * counterpart as one op: the reference's linear_f16 twice, then
+ * gated_silu_mul_f16, gated_mlp.metal:12-41):
+ *   out = silu(x @ w_gate^T) * (x @ w_up^T)
+ * x FP16 [tokens, d] row-major; w_gate_up FP16 [2h, d] with w_gate in rows
+ * 0..h-1 and w_up in rows h..2h-1 (the nn.Linear weight layout); out FP16
+ * [tokens, h].  FP32 accumulation; the gate is applied to the FP32
+ * accumulators and rounded once.  d and h multiples of 8, pointers 16-byte
+ * aligned.  Needs a compute capability 10.x GPU. */
+int mamba_gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h,
+                       void *stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

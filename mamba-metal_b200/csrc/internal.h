@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cstdint>
 
@@ -17,6 +18,7 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
 int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
                         float *h_in, cudaStream_t st);
 unsigned device_error_flags(bool clear);
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st);
 
 // conv.cu
@@ -36,6 +38,14 @@ int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const f
              const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
              const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
              int xd, int dd, int bd, cudaStream_t st);
+
+// carries.cu
+int propagate_tile_carries(float *carries, int num_tiles, int64_t width, float *total, cudaStream_t st);
+int gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int dtype, cudaStream_t st);
+
+// gated_mlp.cu
+int gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h, cudaStream_t st);
+unsigned gemm_error_flags(bool clear);
 
 // init.cu
 uint64_t fill_key(uint64_t seed, int layer, int tag);

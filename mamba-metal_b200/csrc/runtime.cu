@@ -845,7 +845,11 @@ void mamba_destroy_state(MambaStateHandle *s) { delete s; }
 
 const char *mamba_last_error(void) { return mb::last_error(); }
 
-unsigned mamba_device_status(int clear) { return mb::device_error_flags(clear != 0); }
+unsigned mamba_device_status(int clear) {
+    const unsigned scan = mb::device_error_flags(clear != 0);
+    const unsigned gemm = mb::gemm_error_flags(clear != 0);
+    return (scan == ~0u || gemm == ~0u) ? ~0u : (scan | gemm);
+}
 
 int mamba_dt_rank(const MambaConfig *cfg) { return cfg ? (cfg->d_model + 15) / 16 : -1; }
 
@@ -1014,6 +1018,22 @@ int mamba_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols
     mb::clear_error();
     return mb::rmsnorm(x, w, y, rows, cols, eps, in_dtype, out_dtype, static_cast<cudaStream_t>(stream)) ? -1
                                                                                                         : 0;
+}
+
+int mamba_propagate_tile_carries(float *carries, int num_tiles, int64_t width, float *total, void *stream) {
+    mb::clear_error();
+    return mb::propagate_tile_carries(carries, num_tiles, width, total, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h,
+                       void *stream) {
+    mb::clear_error();
+    return mb::gated_mlp_up(x, w_gate_up, out, tokens, d, h, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int dtype, void *stream) {
+    mb::clear_error();
+    return mb::gated_silu_mul(gate, up, out, n, dtype, static_cast<cudaStream_t>(stream)) ? -1 : 0;
 }
 
 }  // extern "C"

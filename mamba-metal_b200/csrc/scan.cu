@@ -478,6 +478,9 @@ __global__ void scan_compose_prefix_kernel(const float *__restrict__ PH, int ran
 }
 
 // ---- host side ------------------------------------------------------------------
+}  // namespace
+
+// The driver's tensor-map encoder, looked up once per process.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -490,6 +493,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     });
     return fn;
 }
+
+namespace {
 
 // 3-D map over a [batch, L, dim0] tensor with stride 1 along dim0; box
 // [1, TT, box0].  False when the layout does not meet the TMA rules

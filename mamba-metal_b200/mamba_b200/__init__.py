@@ -110,6 +110,9 @@ _PROTOTYPES = {
                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "mamba_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_float, c_int, c_int,
                               c_void_p]),
+    "mamba_propagate_tile_carries": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_void_p]),
+    "mamba_gated_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_void_p]),
+    "mamba_gated_mlp_up": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int, c_void_p]),
 }
 
 _lib = None
@@ -209,13 +212,14 @@ class Model:
 
     def __init__(self, d_model, d_state=16, d_conv=4, expand=2, n_layer=1, dtype=F16):
         self.cfg = MambaConfig(d_model, d_state, d_conv, expand, n_layer, dtype)
-        self._h = lib().mamba_create(ctypes.byref(self.cfg))
+        self._lib = lib()  # kept for close() during interpreter shutdown
+        self._h = self._lib.mamba_create(ctypes.byref(self.cfg))
         if not self._h:
             raise MambaError("mamba_create failed: " + last_error())
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().mamba_destroy(self._h)
+            self._lib.mamba_destroy(self._h)
             self._h = None
 
     def __del__(self):
@@ -274,7 +278,8 @@ class Model:
 class State:
     def __init__(self, model, batch):
         self.model = model
-        self._h = lib().mamba_create_state(model.handle, batch)
+        self._lib = lib()
+        self._h = self._lib.mamba_create_state(model.handle, batch)
         if not self._h:
             raise MambaError("mamba_create_state failed: " + last_error())
         self.batch = batch
@@ -284,7 +289,7 @@ class State:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().mamba_destroy_state(self._h)
+            self._lib.mamba_destroy_state(self._h)
             self._h = None
 
     def __del__(self):
@@ -474,3 +479,43 @@ def rmsnorm(x, w=None, eps=1e-5, out_dtype=None, y=None, stream=None):
     _check(lib().mamba_rmsnorm(_ptr(x), _ptr(w), _ptr(y), rows, cols, eps, _dt(x), _dt(y),
                                _stream(stream)), "mamba_rmsnorm")
     return y
+
+
+def propagate_tile_carries(carries, total=None, stream=None):
+    """carries: contiguous FP32 [num_tiles, width, 2] (a, b) pairs, replaced in
+    place by their exclusive prefixes; returns the inclusive total
+    [width, 2] (prefix_scan.metal:19-40)."""
+    torch = _torch()
+    assert carries.is_contiguous() and carries.dtype == torch.float32 and carries.shape[-1] == 2
+    nt, width = carries.shape[0], carries.shape[1]
+    if total is None:
+        total = torch.empty((width, 2), dtype=torch.float32, device=carries.device)
+    _check(lib().mamba_propagate_tile_carries(_ptr(carries), nt, width, _ptr(total), _stream(stream)),
+           "mamba_propagate_tile_carries")
+    return total
+
+
+def gated_mlp_up(x, w_gate_up, out=None, stream=None):
+    """silu(x @ w_gate^T) * (x @ w_up^T) on the tensor cores.  x FP16
+    [tokens, d]; w_gate_up FP16 [2h, d] (gate rows, then up rows)."""
+    torch = _torch()
+    assert x.dtype == torch.float16 and w_gate_up.dtype == torch.float16
+    assert x.is_contiguous() and w_gate_up.is_contiguous()
+    tokens, d = x.shape
+    h = w_gate_up.shape[0] // 2
+    assert w_gate_up.shape == (2 * h, d)
+    if out is None:
+        out = torch.empty((tokens, h), dtype=torch.float16, device=x.device)
+    _check(lib().mamba_gated_mlp_up(_ptr(x), _ptr(w_gate_up), _ptr(out), tokens, d, h, _stream(stream)),
+           "mamba_gated_mlp_up")
+    return out
+
+
+def gated_silu_mul(gate, up, out=None, stream=None):
+    """silu(gate) * up elementwise (contiguous, same dtype)."""
+    assert gate.is_contiguous() and up.is_contiguous() and gate.shape == up.shape
+    if out is None:
+        out = _torch().empty_like(gate)
+    _check(lib().mamba_gated_silu_mul(_ptr(gate), _ptr(up), _ptr(out), gate.numel(), _dt(gate),
+                                      _stream(stream)), "mamba_gated_silu_mul")
+    return out

@@ -48,6 +48,8 @@ def lib():
         L.oracle_ssm_step.argtypes = [_p] * 5 + [_i64, _i64] + [_p] * 5 + [_c] * 3
         L.oracle_rmsnorm.argtypes = [_p, _p, _p, _i64, _c, _f]
         L.oracle_affine_compose.argtypes = [_f, _f, _f, _f, _p, _p]
+        L.oracle_propagate_tile_carries.argtypes = [_p, _c, _i64, _p]
+        L.oracle_gated_silu_mul.argtypes = [_p, _p, _p, _i64]
         _lib = L
     return _lib
 
@@ -172,6 +174,35 @@ def affine_compose(t2, t1):
     a, b = _f(), _f()
     lib().oracle_affine_compose(t2[0], t2[1], t1[0], t1[1], ctypes.byref(a), ctypes.byref(b))
     return a.value, b.value
+
+
+def propagate_tile_carries(carries):
+    """carries [num_tiles, width, 2] FP32 (a, b) pairs -> (exclusive prefixes
+    of the same shape, inclusive total [width, 2]); prefix_scan.metal:19-40."""
+    c = np.array(carries, dtype=np.float32, order="C", copy=True)
+    nt, width = c.shape[0], c.shape[1]
+    total = np.empty((width, 2), np.float32)
+    lib().oracle_propagate_tile_carries(_ptr(c), nt, width, _ptr(total))
+    return c, total
+
+
+def gated_silu_mul(gate, up):
+    """silu(gate) * up elementwise in FP32 (gated_mlp.metal:14-26)."""
+    g, u = _f32(gate), _f32(up)
+    assert g.shape == u.shape
+    out = np.empty_like(g)
+    lib().oracle_gated_silu_mul(_ptr(g), _ptr(u), _ptr(out), g.size)
+    return out
+
+
+def gated_mlp_up(x, w_gate, w_up):
+    """silu(x @ w_gate^T) * (x @ w_up^T) with FP32 products (the two
+    projections gated_mlp.metal:13 assumes done, then its gate).
+    x [T, D]; w_gate, w_up [H, D]."""
+    x, wg, wu = (np.asarray(a, dtype=np.float64) for a in (x, w_gate, w_up))
+    g = (x @ wg.T).astype(np.float32)
+    u = (x @ wu.T).astype(np.float32)
+    return gated_silu_mul(g, u)
 
 
 def causal_conv1d(x, w, bias=None, silu=True):

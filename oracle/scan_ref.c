@@ -27,6 +27,11 @@
  *                              its pair-layout bug fixed): chunk summaries
  *                              (prod a, h_end from zero) and their exclusive
  *                              composition.
+ *   oracle_propagate_tile_carries
+ *                              Sources/Kernels/prefix_scan.metal:19-40 (in-place
+ *                              exclusive scan of interleaved (a, b) tile
+ *                              carries, layout bug fixed)
+ *   oracle_gated_silu_mul      Sources/Kernels/gated_mlp.metal:14-41
  *
  * Parity pin: tests/test_oracle.py checks oracle_selective_scan bit-exactly
  * against golden vectors written by the reference's own selective_scan_cpu
@@ -336,6 +341,48 @@ int oracle_rmsnorm(const float *x, const float *w, float *y, int64_t rows,
             if (w) v *= w[i];
             y[r * N + i] = v;
         }
+    }
+    return 0;
+}
+
+/* Exclusive propagation of tile carries, restating the intent of
+ * propagate_tile_carries_f32 (prefix_scan.metal:19-40) with its pair layout
+ * fixed: carries is [num_tiles, width, 2], pair p of tile t at
+ * (t*width + p)*2 as (a, b).  In place, tile t's pair becomes the
+ * composition of tiles 0..t-1 (identity (1, 0) for tile 0), composed as
+ * compose(cur, acc) (prefix_scan.metal:12-14, selective_scan_cpu.hpp:17-19).
+ * total ([width, 2]) receives the composition of all tiles when not NULL. */
+int oracle_propagate_tile_carries(float *carries, int num_tiles, int64_t width,
+                                  float *total)
+{
+    for (int64_t p = 0; p < width; ++p) {
+        float acc_a = 1.0f, acc_b = 0.0f;
+        for (int t = 0; t < num_tiles; ++t) {
+            float *pr = carries + ((int64_t)t * width + p) * 2;
+            const float a = pr[0], b = pr[1];
+            float na, nb;
+            oracle_affine_compose(a, b, acc_a, acc_b, &na, &nb);
+            pr[0] = acc_a;
+            pr[1] = acc_b;
+            acc_a = na;
+            acc_b = nb;
+        }
+        if (total) {
+            total[2 * p] = acc_a;
+            total[2 * p + 1] = acc_b;
+        }
+    }
+    return 0;
+}
+
+/* SwiGLU gate, restating gated_silu_mul_f32 (gated_mlp.metal:14-26):
+ * out = g / (1 + exp(-g)) * u, elementwise over n values. */
+int oracle_gated_silu_mul(const float *gate, const float *up, float *out, int64_t n)
+{
+    for (int64_t i = 0; i < n; ++i) {
+        const float g = gate[i];
+        const float s = g / (1.0f + expf(-g));
+        out[i] = s * up[i];
     }
     return 0;
 }

@@ -136,3 +136,44 @@ def test_rmsnorm_fp16_input_no_weight(cuda):
     y = mb.rmsnorm(dev(x, torch.float16), None, 1e-5)
     torch.cuda.synchronize()
     assert err(y, y_ref) < 1e-3
+
+
+@pytest.mark.parametrize("nt,width", [(1, 1), (5, 300), (64, 4096), (0, 7), (129, 33)])
+def test_propagate_tile_carries_bitwise(cuda, nt, width):
+    """Exclusive carry propagation equals the oracle bit for bit (same
+    separately rounded products and sums)."""
+    rng = np.random.default_rng(nt * 1000 + width)
+    car = np.stack([rng.uniform(0.5, 1.0, (nt, width)), rng.standard_normal((nt, width))], -1)
+    car = car.astype(np.float32)
+    ex_ref, tot_ref = oracle.propagate_tile_carries(car)
+    c = torch.from_numpy(car).cuda()
+    tot = mb.propagate_tile_carries(c)
+    torch.cuda.synchronize()
+    assert np.array_equal(c.cpu().numpy(), ex_ref)
+    assert np.array_equal(tot.cpu().numpy(), tot_ref)
+
+
+def test_propagate_tile_carries_rejects_misaligned(cuda):
+    c = torch.zeros(2 * 4 * 2 + 1, device="cuda")
+    L = mb.lib()
+    assert L.mamba_propagate_tile_carries(c.data_ptr() + 4, 2, 4, None, None) == -1
+    assert "aligned" in mb.last_error()
+
+
+@pytest.mark.parametrize("n", [1, 7, 4096, 100003])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-6), (torch.float16, 1e-3)])
+def test_gated_silu_mul(cuda, n, dtype, tol):
+    rng = np.random.default_rng(n)
+    g = (rng.standard_normal(n) * 4).astype(np.float32)
+    u = rng.standard_normal(n).astype(np.float32)
+    if dtype == torch.float16:
+        g, u = r16(g), r16(u)
+    want = oracle.gated_silu_mul(g, u)
+    tg, tu = dev(g, dtype), dev(u, dtype)
+    out = mb.gated_silu_mul(tg, tu)
+    # unaligned views take the scalar path
+    out_off = mb.gated_silu_mul(tg[1:], tu[1:]) if n > 1 else None
+    torch.cuda.synchronize()
+    assert err(out, want) < tol
+    if out_off is not None:
+        assert err(out_off, want[1:]) < tol

@@ -206,3 +206,61 @@ def test_block_step_matches_block_forward():
                            for t in range(L)], 1)
         tol = 1e-5 if act == block_ref.F32 else 2e-3
         assert oracle.normwise_rel_err(y_step, y_fwd) < tol
+
+
+def _propagate_loop(carries):
+    """Pure-Python restatement of propagate_tile_carries_f32
+    (prefix_scan.metal:19-40) with the documented [tiles, width, 2] layout:
+    each tile's pair is replaced by the composition of the tiles before it."""
+    c = np.array(carries, np.float32, copy=True)
+    nt, width = c.shape[:2]
+    total = np.empty((width, 2), np.float32)
+    for p in range(width):
+        acc = (np.float32(1), np.float32(0))
+        for t in range(nt):
+            a, b = c[t, p]
+            c[t, p] = acc
+            acc = (np.float32(a * acc[0]), np.float32(np.float32(a * acc[1]) + b))
+        total[p] = acc
+    return c, total
+
+
+def test_tile_carries_restatement():
+    rng = np.random.default_rng(5)
+    for nt, width in [(1, 3), (7, 5), (33, 17), (0, 4)]:
+        car = np.stack([rng.uniform(0.5, 1.0, (nt, width)), rng.standard_normal((nt, width))], -1)
+        car = car.astype(np.float32)
+        ex, tot = oracle.propagate_tile_carries(car)
+        ex_loop, tot_loop = _propagate_loop(car)
+        assert np.array_equal(ex, ex_loop) and np.array_equal(tot, tot_loop)
+        if nt:
+            assert np.array_equal(ex[0], np.tile(np.float32([1, 0]), (width, 1)))
+        else:
+            assert np.array_equal(tot, np.tile(np.float32([1, 0]), (width, 1)))
+
+
+def test_tile_carries_of_chunk_summaries_give_final_state():
+    """Chunk summaries (P, H) of a scan, laid out as [tiles, B*D*N, 2] pairs
+    and propagated, give every chunk's entering state (from zero) and, as the
+    total, the scan's final state."""
+    rng = np.random.default_rng(6)
+    bsz, L, D, N = 2, 64, 8, 16
+    x, dr, B, C, A, Dk = _rand_scan_inputs(rng, bsz, L, D, N)
+    _, h_full = oracle.scan(x, dr, B, C, A, Dk)
+    bounds = [0, 16, 32, 48, 64]
+    pairs = []
+    for t0, t1 in zip(bounds[:-1], bounds[1:]):
+        P, H = oracle.scan_chunk_summary(x, dr, B, A, t0=t0, t1=t1)
+        pairs.append(np.stack([P.reshape(-1), H.reshape(-1)], -1))
+    ex, tot = oracle.propagate_tile_carries(np.stack(pairs))
+    assert oracle.normwise_rel_err(tot[:, 1].reshape(bsz, D, N), h_full) < 1e-5
+    _, h_mid = oracle.scan(x[:, :32], dr[:, :32], B[:, :32], C[:, :32], A, Dk)
+    assert oracle.normwise_rel_err(ex[2, :, 1].reshape(bsz, D, N), h_mid) < 1e-5
+
+
+def test_gated_silu_mul_restatement():
+    rng = np.random.default_rng(7)
+    g = (rng.standard_normal(1001) * 4).astype(np.float32)
+    u = rng.standard_normal(1001).astype(np.float32)
+    want = g / (np.float32(1) + np.exp(-g)) * u
+    np.testing.assert_allclose(oracle.gated_silu_mul(g, u), want, rtol=1e-6, atol=1e-7)
