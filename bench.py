@@ -22,6 +22,11 @@ Workloads (synthetic inputs, random-init weights; no datasets involved):
                    sequence is split across the N ranks with one all-gather
                    of the (P, H) chunk carries; value = algorithmic GB/s.
 
+  mlp              fused SwiGLU up-projection silu(x Wg^T) * (x Wu^T) on the
+                   tensor cores (mamba_gated_mlp_up), 262144 tokens (batch 64
+                   x L 4096), d 2048, h 4096, FP16 in/out, FP32 accumulation;
+                   tokens split across ranks; value = TFLOP/s of the job.
+
 One process per GPU; for N > 1 launch with torchrun (RANK/LOCAL_RANK/
 WORLD_SIZE/MASTER_* from the environment).  Rank 0 prints one JSON line.
 `--impl reference` times the reference's CPU implementation of the same
@@ -48,6 +53,7 @@ STACK = dict(d_model=2048, d_state=16, d_conv=4, expand=2, n_layer=48, batch=64,
 BLOCK = dict(d_model=768, d_state=16, d_conv=4, expand=2, n_layer=1, batch=8, seqlen=2048)
 DECODE = dict(d_model=2560, d_state=16, d_conv=4, expand=2, n_layer=64, batch=256, decode_steps=1024)
 SCAN = dict(batch=1, d_inner=2048, d_state=16, seqlen=131072)
+MLP = dict(tokens=262144, d=2048, h=4096)
 METRIC = "selective-scan HBM GB/s (% peak) and block fwd tokens/s at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 
@@ -312,6 +318,19 @@ def run_stack(args, world, rank, local, C=STACK):
     peak, peak_src = peaks()
     kernels = sum(v[2] for v in prof.values())
     breakdown = {k: round(v[0] / max(v[1], 1), 4) for k, v in prof.items()}
+    # DRAM traffic per launch: the committed ncu figure for the batch-64
+    # stack launch, scaled by the (b, t, d) units of this launch.
+    traffic = None
+    if C is STACK and committed_traffic("selective_scan_stack"):
+        traffic = committed_traffic("selective_scan_stack") * (b * L) / (C["batch"] * C["seqlen"])
+    # The scan's compute ceiling: 18 special-function (XU) operations per
+    # (b, t, d) (16 state exponentials, softplus, SiLU) at 16 per clock per
+    # SM, at the median SM clock sampled during the timed region.
+    xu_ops = 18.0 * b * L * D
+    sm_mhz = (clk or {}).get("sm_mhz") or 1965.0
+    xu_peak = 16.0 * torch.cuda.get_device_properties(local).multi_processor_count * sm_mhz * 1e6
+    xu = {"ops_per_launch": xu_ops, "achieved_ops_per_s": xu_ops / per_launch_s, "peak_ops_per_s": xu_peak,
+          "frac": xu_ops / per_launch_s / xu_peak, "sm_mhz": sm_mhz}
 
     # end to end through the reference C API (mamba_forward, host FP32
     # buffers in pinned memory; H2D and D2H inside the timed region)
@@ -360,9 +379,10 @@ def run_stack(args, world, rank, local, C=STACK):
                 "roofline": {"kernel": "selective_scan (fused, gated)", "bound": "hbm",
                              "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_source": peak_src,
-                             "traffic": committed_traffic("selective_scan_stack"),
+                             "traffic": traffic,
                              "algorithmic_bytes_per_launch": scan_bytes,
-                             "avg_launch_ms": per_launch_s * 1e3},
+                             "avg_launch_ms": per_launch_s * 1e3,
+                             "xu_ceiling": xu},
                 "op_ms_per_layer": breakdown,
                 "gpu_launches": kernels,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk}
@@ -495,13 +515,91 @@ def run_scan(args, world, rank, local):
         print(json.dumps(line))
 
 
+def run_mlp(args, world, rank, local):
+    import torch
+    import mamba_b200 as mb
+    T = args.batch * 4096 if args.batch else MLP["tokens"]
+    d, h = MLP["d"], MLP["h"]
+    if T % world:
+        raise SystemExit("tokens not divisible by ranks")
+    t = T // world
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(900 + rank)
+    x = torch.randn((t, d), device="cuda", generator=g).half()
+    w = (torch.randn((2 * h, d), device="cuda", generator=g) * 0.02).half()
+    out = torch.empty((t, h), device="cuda", dtype=torch.float16)
+
+    def step():
+        mb.gated_mlp_up(x, w, out=out, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(world)
+    assert mb.device_status() == 0
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    flop = 2.0 * T * d * 2 * h
+    value = flop * args.steps / (t_ms / 1e3) / 1e12
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty((t, d), dtype=torch.float16, pin_memory=True)
+        hx.copy_(x.cpu())
+        hout = torch.empty((t, h), dtype=torch.float16, pin_memory=True)
+        xs = torch.empty_like(x)
+        for _ in range(2):
+            xs.copy_(hx, non_blocking=True)
+            mb.gated_mlp_up(xs, w, out=out, stream=stream.cuda_stream)
+            hout.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            xs.copy_(hx, non_blocking=True)
+            mb.gated_mlp_up(xs, w, out=out, stream=stream.cuda_stream)
+            hout.copy_(out, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        te = max_over_ranks(e0.elapsed_time(e1), world)
+        e2e = {"value": flop * args.steps / (te / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": t * d * 2, "d2h_bytes_per_step": t * h * 2,
+               "api": "mamba_gated_mlp_up (pinned host FP16 in/out)"}
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = float(pk.get("bf16_tflops", 1590.0))
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16 operands/output, f32 accumulation",
+                "data": "synthetic",
+                "config": {"workload": "gated MLP up-projection (SwiGLU fused): tokens %d, d %d, h %d" % (T, d, h),
+                           "parallelism": "token-sharded dp%d" % world,
+                           "l2": "x (%.1f GB) and out larger than L2" % (T * d * 2 / 1e9)},
+                "roofline": {"kernel": "gated_mlp_up (tcgen05)", "bound": "tensor", "achieved": value / world,
+                             "peak": peak, "unit": "TFLOP/s", "frac": value / world / peak,
+                             "peak_source": "measured" if pk else "fallback", "traffic": None},
+                "gpu_launches": args.steps, "e2e": e2e, "clocks": clk}
+        print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="stack", choices=["stack", "block", "decode", "scan"])
+    ap.add_argument("--workload", default="stack", choices=["stack", "block", "decode", "scan", "mlp"])
     ap.add_argument("--decode-steps", type=int, default=0, help="decode workload: steps timed")
     ap.add_argument("--layers", type=int, default=0, help="override n_layer (reduced runs)")
     ap.add_argument("--batch", type=int, default=0, help="override global batch")
@@ -523,6 +621,8 @@ def main():
     try:
         if args.workload == "scan":
             run_scan(args, world, rank, local)
+        elif args.workload == "mlp":
+            run_mlp(args, world, rank, local)
         elif args.workload == "decode":
             run_decode(args, world, rank, local)
         elif args.workload == "block":
