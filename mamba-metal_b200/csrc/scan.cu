@@ -53,9 +53,23 @@ namespace {
 constexpr int kScanCH = 128;    // channels (= threads) per CTA
 constexpr int kGenTT = 32;      // generic kernel: timesteps per tile
 constexpr int kTmaTT = 16;      // TMA kernel: timesteps per tile
-constexpr int kTmaStages = 3;   // TMA pipeline depth (48 timesteps in flight)
-constexpr int kTmaMinCtas = 5;  // resident CTAs per SM the TMA kernel is built for
-constexpr int kSubTT = 8;       // timesteps per register batch inside a tile
+#ifndef MAMBA_SCAN_STAGES
+#define MAMBA_SCAN_STAGES 3
+#endif
+constexpr int kTmaStages = MAMBA_SCAN_STAGES;  // TMA pipeline depth
+// 4 resident CTAs (16 warps, up to 128 registers per thread) measured
+// faster than 5 (96 registers) or 3: at [64, 4096, 4096] FP16 5.93 ms vs
+// 6.23 and 6.20 ms.
+#ifndef MAMBA_SCAN_MINCTAS
+#define MAMBA_SCAN_MINCTAS 4
+#endif
+constexpr int kTmaMinCtas = MAMBA_SCAN_MINCTAS;  // resident CTAs per SM the TMA kernel is built for
+// Register batch of 4 timesteps (softplus/SiLU of the batch, then its
+// recurrences): 5.93 ms against 6.03 (8), 6.22 (2), 6.54 (16).
+#ifndef MAMBA_SCAN_SUBTT
+#define MAMBA_SCAN_SUBTT 4
+#endif
+constexpr int kSubTT = MAMBA_SCAN_SUBTT;  // timesteps per register batch inside a tile
 constexpr int kChunkAlign = 32; // chunk lengths are multiples of both tile sizes
 
 enum ScanMode { kModeOutput = 0, kModeSummary = 1 };
@@ -453,12 +467,27 @@ __global__ void scan_combine_kernel(const float *__restrict__ P, float *__restri
     const int64_t b = i / DN, r = i % DN;
     float h = h0 ? h0[i] : 0.f;
     float pt = 1.f;
-    for (int c = 0; c < nchunks; ++c) {
-        const int64_t idx = (b * nchunks + c) * DN + r;
-        const float pc = P[idx], hc = H[idx];
-        if (write_hin) H[idx] = h;
-        h = pc * h + hc;
-        pt *= pc;
+    // Loads for 8 chunks are issued before the dependent combine chain, so
+    // the walk is not one HBM round trip per chunk.
+    constexpr int kAhead = 8;
+    for (int c0 = 0; c0 < nchunks; c0 += kAhead) {
+        float pc[kAhead], hc[kAhead];
+#pragma unroll
+        for (int j = 0; j < kAhead; ++j) {
+            if (c0 + j < nchunks) {
+                const int64_t idx = (b * nchunks + c0 + j) * DN + r;
+                pc[j] = P[idx];
+                hc[j] = H[idx];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kAhead; ++j) {
+            if (c0 + j < nchunks) {
+                if (write_hin) H[(b * nchunks + c0 + j) * DN + r] = h;
+                h = pc[j] * h + hc[j];
+                pt *= pc[j];
+            }
+        }
     }
     if (H_total) H_total[i] = h;
     if (P_total) P_total[i] = pt;
@@ -593,9 +622,17 @@ int choose_chunk_len(int batch, int L, int D, int requested) {
         const int c = ceil_div(requested, kChunkAlign) * kChunkAlign;
         return std::min(c, L);
     }
+    // One pass over time costs L steps of one CTA's latency (about 360 SM
+    // cycles per step when a warp has its scheduler to itself); splitting
+    // time into chunks doubles the work (summary + rescan) but spreads it
+    // over idle SMs.  Measured on B200 (FP16, N 16): with at least one CTA
+    // per SM the single pass wins (batch 16 x 4096 channels, L 4096:
+    // 1.79 ms vs 2.75-2.90 ms chunked); below that chunking wins (batch 8
+    // x 1536 channels, L 2048: 0.32-0.33 vs 0.39 ms; batch 1 x 2048,
+    // L 131072: 2.8 vs 24 ms).
     const int64_t ctas = (int64_t)batch * ceil_div(D, kScanCH);
     const int sms = device_sm_count();
-    if (ctas >= 4LL * sms) return L;
+    if (ctas >= sms) return L;
     const int64_t want = ceil_div64(8LL * sms, ctas);
     const int64_t maxc = std::max<int64_t>(1, L / 128);
     const int64_t nc = std::min(want, maxc);
