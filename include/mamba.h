@@ -101,7 +101,9 @@ const char *mamba_last_error(void);
  * clear (0 = none).  Bit 0: a shared-memory pipeline wait inside the
  * selective scan exceeded its 2-second bound, so that call stopped early and
  * its outputs are invalid.  Bit 1: the same for a wait inside
- * mamba_gated_mlp_up.  Waits for the device; clear != 0 resets them. */
+ * mamba_gated_mlp_up.  Bit 2: the same for mamba_linear (and the decode
+ * projections that use it).  Waits for the device; clear != 0 resets
+ * them. */
 unsigned mamba_device_status(int clear);
 
 /* dt_rank used for a config: ceil(d_model / 16). */
@@ -304,6 +306,24 @@ int mamba_propagate_tile_carries(float *carries, int num_tiles, int64_t width, f
  * MAMBA_F16; FP16 computes in FP32 and rounds once). */
 int mamba_gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int dtype,
                          void *stream);
+
+/* Linear layer on the tensor cores (linear_f16, projection.metal:32-49):
+ *   mode 0: y (FP16)  = x @ w^T + bias
+ *   mode 1: y (FP32) += x @ w^T + bias   (accumulate into an FP32 buffer)
+ *   mode 2: y (FP32)  = x @ w^T + bias
+ * x FP16 [rows, k] with row stride ldx elements; w FP16 [n, k] (the
+ * reference's [k, n] weight transposed, i.e. K-major); bias FP32 [n] or
+ * NULL; y row stride ldy elements.  FP32 accumulation.  k and n multiples
+ * of 8, ldx and ldy multiples of 8, pointers 16-byte aligned.  Built for few rows (decode):
+ * K is split across CTAs when the output blocks cannot fill the GPU, which
+ * needs a workspace of mamba_linear_workspace(rows, n, k) bytes (0 when no
+ * split is made; 16-byte aligned) for the FP32 partials, summed in split
+ * order by a second kernel (results do not depend on CTA timing).  Calls
+ * sharing a workspace must not overlap on the GPU.  Needs a compute
+ * capability 10.x GPU. */
+size_t mamba_linear_workspace(int64_t rows, int n, int k);
+int mamba_linear(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t rows,
+                 int n, int k, int mode, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Fused SwiGLU up-projection on the tensor cores (no reference
  * counterpart as one op: the reference's linear_f16 twice, then

@@ -47,6 +47,12 @@ int gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int d
 int gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h, cudaStream_t st);
 unsigned gemm_error_flags(bool clear);
 
+// linear_tc.cu
+size_t linear_workspace_bytes(int64_t M, int N, int K);
+int linear_tc(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t M, int N,
+              int K, int mode, void *ws, size_t ws_bytes, cudaStream_t st);
+unsigned linear_error_flags(bool clear);
+
 // init.cu
 uint64_t fill_key(uint64_t seed, int layer, int tag);
 int fill_random(void *out, int dtype, int64_t n, uint64_t key, int dist, float p0, float p1,

@@ -249,6 +249,7 @@ struct Model {
                                            "' is not sm_100 (compute capability 10.x required)");
         MB_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
         if (const char *g = std::getenv("MAMBA_STEP_GRAPH")) use_graphs = std::atoi(g) != 0;
+        if (const char *t = std::getenv("MAMBA_TC_LINEAR")) tc_linear = std::atoi(t) != 0;
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -289,10 +290,37 @@ struct Model {
     // C[rows, n] (ldc) = A[rows, k] (lda) @ W where W is stored as Wt [n, k];
     // beta = 1 accumulates into C (used for the residual).  C may be FP32
     // while A/W are FP16 (FP32 accumulation in every case).
+    // The projections run on cuBLAS.  MAMBA_TC_LINEAR=1 sends few-row FP16
+    // projections (decode batches, short forwards) to this library's
+    // tcgen05 linear kernel instead; at the decode shapes (256 rows) it is
+    // measured 2-3x slower than cuBLAS (its K splits cannot balance the
+    // output blocks over 148 SMs), so it is off by default.
+    static constexpr int64_t kTcRows = 512;
+    bool tc_linear = false;  // read from MAMBA_TC_LINEAR when the model is created
+    bool tc_linear_enabled() const { return tc_linear; }
+    bool use_tc(int64_t rows, int n, int k, int lda, int ldc) const {
+        return act == MAMBA_F16 && rows <= kTcRows && tc_linear_enabled() && n % 8 == 0 && k % 8 == 0 &&
+               lda % 8 == 0 && ldc % 8 == 0;
+    }
+    // Workspace for the split-K partials of every projection of one layer.
+    size_t linear_ws_need(int64_t rows) const {
+        size_t w = 0;
+        const int shapes[4][4] = {{2 * D, M, M, 2 * D}, {XD, D, D, XD}, {D, R, XD, D}, {M, D, D, M}};
+        for (const auto &sh : shapes)
+            if (use_tc(rows, sh[0], sh[1], sh[2], sh[3])) w = std::max(w, linear_workspace_bytes(rows, sh[0], sh[1]));
+        return w;
+    }
+
     int gemm(cudaStream_t st, int64_t rows, int n, int k, const void *A, int lda, const void *Wt,
-             void *C, int ldc, int c_dtype, float beta) {
+             void *C, int ldc, int c_dtype, float beta, void *lws, size_t lws_bytes) {
         if (rows == 0 || n == 0) return 0;
         MB_CHECK_ARG(rows <= 0x7fffffffLL, "gemm: too many rows");
+        const bool aligned = reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(Wt) % 16 == 0 &&
+                             reinterpret_cast<uintptr_t>(C) % 16 == 0;
+        if (aligned && use_tc(rows, n, k, lda, ldc) && (beta == 0.f || (beta == 1.f && c_dtype == MAMBA_F32))) {
+            const int mode = c_dtype == MAMBA_F16 ? 0 : (beta == 1.f ? 1 : 2);
+            return linear_tc(A, lda, Wt, nullptr, C, ldc, rows, n, k, mode, lws, lws_bytes, st);
+        }
         const cudaDataType at = act == MAMBA_F16 ? CUDA_R_16F : CUDA_R_32F;
         const cudaDataType ct = c_dtype == MAMBA_F16 ? CUDA_R_16F : CUDA_R_32F;
         const float alpha = 1.f;
@@ -311,8 +339,8 @@ struct Model {
     }
 
     struct Arena {
-        void *normed, *xz, *u, *xdbc, *draw, *y, *scan_ws;
-        size_t scan_ws_bytes;
+        void *normed, *xz, *u, *xdbc, *draw, *y, *scan_ws, *lin_ws;
+        size_t scan_ws_bytes, lin_ws_bytes;
     };
 
     MambaScanArgs scan_args(const LayerWeights &w, const Arena &ar, int batch, int L) const {
@@ -358,8 +386,10 @@ struct Model {
         Arena probe{};
         MambaScanArgs sa = scan_args(layers.empty() ? LayerWeights{} : layers[0], probe, batch, L);
         const size_t ws = scan_workspace_bytes(&sa);
+        const size_t lws = linear_ws_need(T);
         size_t need = align_up(T * M * a) + align_up(T * 2 * D * a) + align_up(T * D * a) +
-                      align_up(T * XD * a) + align_up(T * D * a) + align_up(T * D * a) + align_up(ws);
+                      align_up(T * XD * a) + align_up(T * D * a) + align_up(T * D * a) + align_up(ws) +
+                      align_up(lws);
         if (need > arena.bytes) {
             // Work queued on either stream may still read the old arena.
             MB_CUDA_TRY(cudaStreamSynchronize(stream));
@@ -380,6 +410,8 @@ struct Model {
         ar.y = take(T * D * a);
         ar.scan_ws = ws ? take(ws) : nullptr;
         ar.scan_ws_bytes = ws;
+        ar.lin_ws = lws ? take(lws) : nullptr;
+        ar.lin_ws_bytes = lws;
         return 0;
     }
 
@@ -402,7 +434,9 @@ struct Model {
             }
             {
                 OpScope o(prof, MAMBA_OP_IN_PROJ, st, 0);
-                if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f)) return -1;
+                if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f, ar.lin_ws,
+                         ar.lin_ws_bytes))
+                    return -1;
             }
             {
                 OpScope o(prof, MAMBA_OP_CONV, st, 1);
@@ -410,11 +444,13 @@ struct Model {
             }
             {
                 OpScope o(prof, MAMBA_OP_X_PROJ, st, 0);
-                if (gemm(st, T, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, act, 0.f)) return -1;
+                if (gemm(st, T, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
+                    return -1;
             }
             {
                 OpScope o(prof, MAMBA_OP_DT_PROJ, st, 0);
-                if (gemm(st, T, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, act, 0.f)) return -1;
+                if (gemm(st, T, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
+                    return -1;
             }
             {
                 MambaScanArgs sa = scan_args(w, ar, batch, L);
@@ -423,7 +459,8 @@ struct Model {
             }
             {
                 OpScope o(prof, MAMBA_OP_OUT_PROJ, st, 0);
-                if (gemm(st, T, M, D, ar.y, D, w.w_out_t, out, M, MAMBA_F32, 1.f)) return -1;
+                if (gemm(st, T, M, D, ar.y, D, w.w_out_t, out, M, MAMBA_F32, 1.f, ar.lin_ws, ar.lin_ws_bytes))
+                    return -1;
             }
         }
         return 0;
@@ -471,14 +508,16 @@ struct MambaModel {
 namespace mb {
 
 struct StepArena {
-    void *normed, *xz, *u, *xdbc, *draw, *y;
+    void *normed, *xz, *u, *xdbc, *draw, *y, *lin_ws;
+    size_t lin_ws_bytes;
 };
 
 static int ensure_step_arena(Model &m, int rows, StepArena &ar) {
     const size_t a = m.act_size();
     const int64_t T = rows;
+    const size_t lws = m.linear_ws_need(T);
     const size_t need = align_up(T * m.M * a) + align_up(T * 2 * m.D * a) + align_up(T * m.D * a) +
-                        align_up(T * m.XD * a) + align_up(T * m.D * a) + align_up(T * m.D * a);
+                        align_up(T * m.XD * a) + align_up(T * m.D * a) + align_up(T * m.D * a) + align_up(lws);
     if (need > m.step_arena.bytes) {
         MB_CUDA_TRY(cudaStreamSynchronize(m.stream));
         MB_CUDA_TRY(cudaStreamSynchronize(m.cur_stream()));
@@ -496,6 +535,8 @@ static int ensure_step_arena(Model &m, int rows, StepArena &ar) {
     ar.xdbc = take(T * m.XD * a);
     ar.draw = take(T * m.D * a);
     ar.y = take(T * m.D * a);
+    ar.lin_ws = lws ? take(lws) : nullptr;
+    ar.lin_ws_bytes = lws;
     return 0;
 }
 
@@ -518,7 +559,9 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
         }
         {
             OpScope o(pf, MAMBA_OP_IN_PROJ, st, 0);
-            if (m.gemm(st, Bt, 2 * D, m.M, ar.normed, m.M, w.w_in_t, ar.xz, 2 * D, m.act, 0.f)) return -1;
+            if (m.gemm(st, Bt, 2 * D, m.M, ar.normed, m.M, w.w_in_t, ar.xz, 2 * D, m.act, 0.f, ar.lin_ws,
+                       ar.lin_ws_bytes))
+                return -1;
         }
         {
             OpScope o(pf, MAMBA_OP_CONV, st, 1);
@@ -528,11 +571,13 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
         }
         {
             OpScope o(pf, MAMBA_OP_X_PROJ, st, 0);
-            if (m.gemm(st, Bt, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, m.act, 0.f)) return -1;
+            if (m.gemm(st, Bt, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, m.act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
+                return -1;
         }
         {
             OpScope o(pf, MAMBA_OP_DT_PROJ, st, 0);
-            if (m.gemm(st, Bt, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, m.act, 0.f)) return -1;
+            if (m.gemm(st, Bt, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, m.act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
+                return -1;
         }
         {
             OpScope o(pf, MAMBA_OP_SCAN, st, 1);
@@ -544,7 +589,8 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
         }
         {
             OpScope o(pf, MAMBA_OP_OUT_PROJ, st, 0);
-            if (m.gemm(st, Bt, m.M, D, ar.y, D, w.w_out_t, out, m.M, MAMBA_F32, 1.f)) return -1;
+            if (m.gemm(st, Bt, m.M, D, ar.y, D, w.w_out_t, out, m.M, MAMBA_F32, 1.f, ar.lin_ws, ar.lin_ws_bytes))
+                return -1;
         }
     }
     return 0;
@@ -848,7 +894,8 @@ const char *mamba_last_error(void) { return mb::last_error(); }
 unsigned mamba_device_status(int clear) {
     const unsigned scan = mb::device_error_flags(clear != 0);
     const unsigned gemm = mb::gemm_error_flags(clear != 0);
-    return (scan == ~0u || gemm == ~0u) ? ~0u : (scan | gemm);
+    const unsigned lin = mb::linear_error_flags(clear != 0);
+    return (scan == ~0u || gemm == ~0u || lin == ~0u) ? ~0u : (scan | gemm | lin);
 }
 
 int mamba_dt_rank(const MambaConfig *cfg) { return cfg ? (cfg->d_model + 15) / 16 : -1; }
@@ -1023,6 +1070,17 @@ int mamba_rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols
 int mamba_propagate_tile_carries(float *carries, int num_tiles, int64_t width, float *total, void *stream) {
     mb::clear_error();
     return mb::propagate_tile_carries(carries, num_tiles, width, total, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+size_t mamba_linear_workspace(int64_t rows, int n, int k) { return mb::linear_workspace_bytes(rows, n, k); }
+
+int mamba_linear(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t rows,
+                 int n, int k, int mode, void *workspace, size_t workspace_bytes, void *stream) {
+    mb::clear_error();
+    return mb::linear_tc(x, ldx, w, bias, y, ldy, rows, n, k, mode, workspace, workspace_bytes,
+                         static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
 }
 
 int mamba_gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h,

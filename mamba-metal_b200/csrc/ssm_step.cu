@@ -25,7 +25,7 @@ __global__ void __launch_bounds__(128)
                     const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
                     const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
                     const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
-                    Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N) {
+                    Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N, int aligned) {
     constexpr bool PRECISE = std::is_same<Tx, float>::value;
     __shared__ __align__(16) float sBC[2 * NS];  // B[0..NS) then C[0..NS)
     const int b = blockIdx.y;
@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(128)
     float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
     const bool small = load_channel_consts<NS, PRECISE>(A, d, N, true, Ac, kI);
     float *hp = state + ((int64_t)b * D + d) * N;
-    const bool vec = (NS == N) && (NS % 4 == 0);
+    const bool vec = aligned && (NS == N) && (NS % 4 == 0);
     if (vec) {
 #pragma unroll
         for (int i = 0; i < NS / 4; ++i) {
@@ -84,86 +84,122 @@ __global__ void __launch_bounds__(128)
 
 // FP16 fast path: four threads per channel, each owning NS/4 consecutive
 // states, so lane l of a warp reads and writes bytes [16 l, 16 l + 16) of a
-// contiguous 512-byte run (full coalescing) and four times as many threads
-// hide the state latency.  Each state sees exactly the per-state operations
-// of scan_step (fast mode); the four partial sums of C*h are combined with
-// two butterfly shuffles.
-template <int NS, typename Tx, typename Tdt, typename Tbc>
+// contiguous 512-byte run (full coalescing).  Each thread serves R batch
+// rows of its channel: A and 1/A are loaded once, and the R state vectors
+// are all in flight before any is used (with one row per thread too few
+// bytes are in flight per SM to cover HBM latency).  Each state sees exactly
+// the per-state operations of scan_step (fast mode); the four partial sums
+// of C*h are combined with two butterfly shuffles.
+template <int NS, int R, typename Tx, typename Tdt, typename Tbc>
 __global__ void __launch_bounds__(128)
     ssm_step_quad_kernel(const Tx *__restrict__ x, int64_t xrs, const Tdt *__restrict__ delta, int64_t drs,
                          const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
                          const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
                          const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
-                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int D, int N) {
+                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int batch, int D, int N,
+                         int aligned) {
     constexpr int S = NS / 4;  // states per thread
-    __shared__ __align__(16) float sBC[2 * NS];
-    const int b = blockIdx.y;
+    static_assert(R * 2 * NS <= 128, "B/C staging uses one thread per value");
+    __shared__ __align__(16) float sBC[R][2 * NS];
+    const int b0 = blockIdx.y * R;
     const int q = threadIdx.x & 3;
     const int d = blockIdx.x * 32 + (threadIdx.x >> 2);
-    if (threadIdx.x < 2 * NS) {
-        const int j = threadIdx.x;
+    if (threadIdx.x < R * 2 * NS) {
+        const int r = threadIdx.x / (2 * NS), j = threadIdx.x % (2 * NS);
+        const int b = b0 + r;
         float v = 0.f;
-        if (j < NS) {
-            if (j < N) v = ld_f32(Bm + (int64_t)b * bcrs + j);
-        } else if (j - NS < N) {
-            v = ld_f32(Cm + (int64_t)b * bcrs + (j - NS));
+        if (b < batch) {
+            if (j < NS) {
+                if (j < N) v = ld_f32(Bm + (int64_t)b * bcrs + j);
+            } else if (j - NS < N) {
+                v = ld_f32(Cm + (int64_t)b * bcrs + (j - NS));
+            }
         }
-        sBC[j] = v;
+        sBC[r][j] = v;
     }
-    __syncthreads();
-    // Lanes of channels past D stay to the end (every lane of the warp takes
-    // part in the shuffles below); only their memory accesses are skipped.
+    // Lanes of channels past D (and rows past the batch) stay to the end
+    // (every lane of the warp takes part in the shuffles below); only their
+    // memory accesses are skipped.
     const bool valid = d < D;
     const int dd = valid ? d : 0;
-    float ac[S], kI[S], h[S];
-#pragma unroll
-    for (int j = 0; j < S; ++j) {
-        const int n = q * S + j;
-        const float a = (valid && n < N) ? A[(int64_t)dd * N + n] : 0.f;
-        ac[j] = a * kLog2e;
-        kI[j] = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
-        h[j] = 0.f;
-    }
-    float *hp = state + ((int64_t)b * D + dd) * N + q * S;
-    const bool vec = (NS == N) && (S == 4);
-    if (valid) {
-        if (vec) {
-            const float4 v = *reinterpret_cast<const float4 *>(hp);
-            h[0] = v.x;
-            h[S > 1 ? 1 : 0] = v.y;
-            h[S > 2 ? 2 : 0] = v.z;
-            h[S > 3 ? 3 : 0] = v.w;
-        } else {
-#pragma unroll
-            for (int j = 0; j < S; ++j) h[j] = q * S + j < N ? hp[j] : 0.f;
-        }
-    }
-    const float xv = valid ? ld_f32(x + (int64_t)b * xrs + dd) : 0.f;
-    float draw = valid ? ld_f32(delta + (int64_t)b * drs + dd) : 0.f;
-    if (dt_bias && valid) draw = __fadd_rn(draw, dt_bias[dd]);
-    const float dt = softplus_fast(draw);
-    float yp = 0.f;
-#pragma unroll
-    for (int j = 0; j < S; ++j) {
-        const int n = q * S + j;
-        const float a = ex2_approx(dt * ac[j]);
-        h[j] = state_update(a, xv * sBC[n], kI[j], dt, h[j]);
-        yp = fmaf(sBC[NS + n], h[j], yp);
-    }
-    yp += __shfl_xor_sync(0xffffffffu, yp, 1);
-    yp += __shfl_xor_sync(0xffffffffu, yp, 2);
-    if (!valid) return;
+    // 16-byte vector accesses to A and the state when both are 16-byte
+    // aligned (checked on the host) and the state rows are exactly NS long.
+    const bool vec = aligned && (NS == N) && (S == 4);
+    float ac[S], kI[S];
     if (vec) {
-        *reinterpret_cast<float4 *>(hp) = make_float4(h[0], h[S > 1 ? 1 : 0], h[S > 2 ? 2 : 0], h[S > 3 ? 3 : 0]);
+        const float4 a4 = valid ? *reinterpret_cast<const float4 *>(A + (int64_t)dd * N + q * S)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+            ac[j] = av[j & 3] * kLog2e;
+            kI[j] = fabsf(av[j & 3]) > 1e-6f ? 1.0f / av[j & 3] : 0.f;
+        }
     } else {
 #pragma unroll
-        for (int j = 0; j < S; ++j)
-            if (q * S + j < N) hp[j] = h[j];
+        for (int j = 0; j < S; ++j) {
+            const int n = q * S + j;
+            const float a = (valid && n < N) ? A[(int64_t)dd * N + n] : 0.f;
+            ac[j] = a * kLog2e;
+            kI[j] = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
+        }
     }
-    if (q == 0) {
-        const float dsk = Dskip ? Dskip[d] : 0.f;
-        const float gate = z ? silu_fast(ld_f32(z + (int64_t)b * zrs + d)) : 1.f;
-        y[(int64_t)b * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv, yp) * gate);
+    float h[R][S], xv[R], draw[R];
+    bool rv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int b = b0 + r;
+        rv[r] = valid && b < batch;
+        const int bb = rv[r] ? b : 0;
+        const float *hp = state + ((int64_t)bb * D + dd) * N + q * S;
+#pragma unroll
+        for (int j = 0; j < S; ++j) h[r][j] = 0.f;
+        if (rv[r]) {
+            if (vec) {
+                const float4 v = *reinterpret_cast<const float4 *>(hp);
+                h[r][0] = v.x;
+                h[r][S > 1 ? 1 : 0] = v.y;
+                h[r][S > 2 ? 2 : 0] = v.z;
+                h[r][S > 3 ? 3 : 0] = v.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < S; ++j) h[r][j] = q * S + j < N ? hp[j] : 0.f;
+            }
+        }
+        xv[r] = rv[r] ? ld_f32(x + (int64_t)bb * xrs + dd) : 0.f;
+        draw[r] = rv[r] ? ld_f32(delta + (int64_t)bb * drs + dd) : 0.f;
+    }
+    const float bias = (dt_bias && valid) ? dt_bias[dd] : 0.f;
+    __syncthreads();  // sBC
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float dt = softplus_fast(dt_bias ? __fadd_rn(draw[r], bias) : draw[r]);
+        float yp = 0.f;
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+            const int n = q * S + j;
+            const float a = ex2_approx(dt * ac[j]);
+            h[r][j] = state_update(a, xv[r] * sBC[r][n], kI[j], dt, h[r][j]);
+            yp = fmaf(sBC[r][NS + n], h[r][j], yp);
+        }
+        yp += __shfl_xor_sync(0xffffffffu, yp, 1);
+        yp += __shfl_xor_sync(0xffffffffu, yp, 2);
+        if (!rv[r]) continue;
+        const int b = b0 + r;
+        float *hp = state + ((int64_t)b * D + d) * N + q * S;
+        if (vec) {
+            *reinterpret_cast<float4 *>(hp) =
+                make_float4(h[r][0], h[r][S > 1 ? 1 : 0], h[r][S > 2 ? 2 : 0], h[r][S > 3 ? 3 : 0]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+                if (q * S + j < N) hp[j] = h[r][j];
+        }
+        if (q == 0) {
+            const float dsk = Dskip ? Dskip[d] : 0.f;
+            const float gate = z ? silu_fast(ld_f32(z + (int64_t)b * zrs + d)) : 1.f;
+            y[(int64_t)b * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv[r], yp) * gate);
+        }
     }
 }
 
@@ -172,20 +208,35 @@ int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, cons
                 const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
                 const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
                 int N, cudaStream_t st) {
+    const int aligned = reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(state) % 16 == 0;
     if (!std::is_same<Tx, float>::value) {
-        // Four threads per channel, 32 channels per CTA.
-        dim3 grid(ceil_div(D, 32), batch);
-        ssm_step_quad_kernel<NS, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
-            static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
-            static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
-            static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, D, N);
+        // Four threads per channel, 32 channels per CTA, R batch rows per
+        // thread (fewer rows when the batch is small, to keep CTAs many).
+#ifndef MAMBA_STEP_ROWS
+#define MAMBA_STEP_ROWS 4
+#endif
+        constexpr int R = MAMBA_STEP_ROWS;
+        const bool many = (int64_t)ceil_div(D, 32) * ceil_div(batch, R) >= 2LL * device_sm_count();
+        if (many) {
+            dim3 grid(ceil_div(D, 32), ceil_div(batch, R));
+            ssm_step_quad_kernel<NS, R, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
+                static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
+                static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
+                static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, batch, D, N, aligned);
+        } else {
+            dim3 grid(ceil_div(D, 32), batch);
+            ssm_step_quad_kernel<NS, 1, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
+                static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
+                static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
+                static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, batch, D, N, aligned);
+        }
         return launch_status("ssm_step kernel");
     }
     dim3 grid(ceil_div(D, 128), batch);
     ssm_step_kernel<NS, Tx, Tdt, Tbc><<<grid, 128, 0, st>>>(
         static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
         static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
-        static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, D, N);
+        static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, D, N, aligned);
     return launch_status("ssm_step kernel");
 }
 

@@ -113,6 +113,9 @@ _PROTOTYPES = {
     "mamba_propagate_tile_carries": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_void_p]),
     "mamba_gated_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_void_p]),
     "mamba_gated_mlp_up": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int, c_void_p]),
+    "mamba_linear_workspace": (c_size, [c_i64, c_int, c_int]),
+    "mamba_linear": (c_int, [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_int, c_int, c_int,
+                             c_void_p, c_size, c_void_p]),
 }
 
 _lib = None
@@ -493,6 +496,27 @@ def propagate_tile_carries(carries, total=None, stream=None):
     _check(lib().mamba_propagate_tile_carries(_ptr(carries), nt, width, _ptr(total), _stream(stream)),
            "mamba_propagate_tile_carries")
     return total
+
+
+def linear(x, w, bias=None, y=None, mode=0, workspace=None, stream=None):
+    """y = x @ w^T (+ bias) on the tensor cores.  x FP16 [rows, k] (row
+    stride any multiple of 8); w FP16 [n, k]; mode 0 -> y FP16, 1 -> y FP32
+    += result, 2 -> y FP32 = result.  A workspace is allocated when none is
+    given and the call splits K."""
+    torch = _torch()
+    assert x.dtype == torch.float16 and w.dtype == torch.float16
+    assert x.stride(1) == 1 and w.is_contiguous()
+    rows, k = x.shape
+    n = w.shape[0]
+    if y is None:
+        y = torch.empty((rows, n), dtype=torch.float16 if mode == 0 else torch.float32, device=x.device)
+    need = lib().mamba_linear_workspace(rows, n, k)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    ws_ptr, ws_len = (_ptr(workspace), workspace.numel()) if workspace is not None else (None, 0)
+    _check(lib().mamba_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), rows, n, k, mode,
+                              ws_ptr, ws_len, _stream(stream)), "mamba_linear")
+    return y
 
 
 def gated_mlp_up(x, w_gate_up, out=None, stream=None):

@@ -195,6 +195,15 @@ def gated_silu_mul(gate, up):
     return out
 
 
+def linear(x, w, bias=None):
+    """y = x @ w^T + bias in float64 (linear_f32/_f16, projection.metal:25-29,
+    whose W is [K, N]; here w is that matrix transposed, [N, K])."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y
+
+
 def gated_mlp_up(x, w_gate, w_up):
     """silu(x @ w_gate^T) * (x @ w_up^T) with FP32 products (the two
     projections gated_mlp.metal:13 assumes done, then its gate).

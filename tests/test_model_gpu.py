@@ -185,3 +185,27 @@ def test_graph_replayed_decode_equals_plain_launches(cuda, monkeypatch):
     sp.step_device(dev_in.data_ptr(), out_b.data_ptr())
     torch.cuda.synchronize()
     assert torch.equal(out_a, out_b)
+
+
+def test_decode_with_tcgen05_projections_matches_cublas(cuda, monkeypatch):
+    """MAMBA_TC_LINEAR=1 runs the decode projections (batch rows <= 512) on
+    the library's tcgen05 linear kernel; the steps agree with the cuBLAS
+    model within the FP16 tolerance."""
+    rng = np.random.default_rng(108)
+    cfg = mb.MambaConfig(256, 16, 4, 2, 2, mb.F16)
+    layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
+    blob = mb.make_weight_blob(cfg, layers)
+    monkeypatch.setenv("MAMBA_TC_LINEAR", "0")
+    ref = mb.Model(256, 16, 4, 2, 2, mb.F16)
+    monkeypatch.setenv("MAMBA_TC_LINEAR", "1")
+    tc = mb.Model(256, 16, 4, 2, 2, mb.F16)
+    ref.load_weights(blob)
+    tc.load_weights(blob)
+    sr, st = ref.create_state(40), tc.create_state(40)
+    toks = rng.standard_normal((6, 40, 256)).astype(np.float32)
+    for t in range(6):
+        a, b = sr.step(toks[t]), st.step(toks[t])
+        assert oracle.normwise_rel_err(b - toks[t], a - toks[t]) < 2e-3, t
+    h = rng.standard_normal((2, 50, 256)).astype(np.float32)
+    assert oracle.normwise_rel_err(tc.forward(h) - h, ref.forward(h) - h) < 2e-3
+    assert mb.device_status() == 0

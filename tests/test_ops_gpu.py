@@ -177,3 +177,30 @@ def test_gated_silu_mul(cuda, n, dtype, tol):
     assert err(out, want) < tol
     if out_off is not None:
         assert err(out_off, want[1:]) < tol
+
+
+@pytest.mark.parametrize("misalign", [False, True])
+def test_ssm_step_multirow_kernel(cuda, misalign):
+    """Large enough to take the several-rows-per-thread FP16 decode kernel:
+    2048 channels x batch 19 (the last row group holds 3 rows).  With A and
+    the state 4 bytes off a 16-byte boundary the kernel uses scalar accesses
+    and must give the same results."""
+    bsz, L, D, N = 19, 3, 2048, 16
+    x, dr, B, C, z, A, Dk = scan_inputs(21, bsz, L, D, N)
+    x, dr, B, C, z = map(r16, (x, dr, B, C, z))
+    bias = np.random.default_rng(1).normal(0, 0.5, D).astype(np.float32)
+    st_ref = np.zeros((bsz, D, N), np.float32)
+    tA_buf = torch.zeros(D * N + 1, device="cuda")
+    st_buf = torch.zeros(bsz * D * N + 1, device="cuda")
+    off = 1 if misalign else 0
+    tA = tA_buf[off:off + D * N].view(D, N)
+    tA.copy_(torch.from_numpy(A))
+    st = st_buf[off:off + bsz * D * N].view(bsz, D, N)
+    tD, tb = dev(Dk), dev(bias)
+    tx, tdr, tB, tC, tz = (dev(a, torch.float16) for a in (x, dr, B, C, z))
+    for t in range(L):
+        yr = oracle.ssm_step(x[:, t], dr[:, t], B[:, t], C[:, t], A, Dk, st_ref, z=z[:, t], dt_bias=bias)
+        y = mb.ssm_step(tx[:, t], tdr[:, t], tA, tB[:, t], tC[:, t], st, D=tD, z=tz[:, t], dt_bias=tb)
+        torch.cuda.synchronize()
+        assert err(y, yr) < TOL16
+    assert err(st, st_ref) < TOL32
