@@ -455,6 +455,243 @@ __global__ void __launch_bounds__(CH, kTmaMinCtas)
     if (dvalid) write_epilogue<NS>(p, SUMMARY, b, chunk, d, t_end, h, P);
 }
 
+// ---- four lanes per channel (few channels, single pass) ----------------------
+// For problems with fewer 128-channel CTAs than SMs, one thread per channel
+// is bound by the latency of a timestep, and splitting time into chunks
+// doubles the work.  Here four lanes share a channel, each holding NS/4 of
+// its states, so a timestep's exponentials are spread over four lanes and
+// four times as many warps are in flight.  A CTA serves 32 channels of one
+// batch row; tiles of x, delta, z ([TT steps x 32 channels]) and B, C come
+// through the same 3-stage TMA ring as the one-thread kernel, B and C
+// converted once per tile to FP32.  Each lane evaluates the timestep's
+// softplus and SiLU itself (no exchange needed), updates its states with
+// state_update (the fast path of the one-thread kernel) and the four partial
+// sums of C*h are combined with two butterfly shuffles.  Output mode only.
+constexpr int kQuadCPB = 32;  // channels per CTA
+
+// One timestep of one lane's S states (S even: packed pairs, as scan_step):
+// bq, cq point at this lane's B and C values in the FP32 tile.
+template <int S, bool SMALLA>
+__device__ __forceinline__ float quad_states(float x, float dt, const float *__restrict__ bq,
+                                             const float *__restrict__ cq, float2 *h, const float2 *ac,
+                                             const float2 *kI) {
+    static_assert(S % 2 == 0, "packed pairs");
+    float2 Bv[S / 2], Cv[S / 2];
+    if (S == 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(bq), c4 = *reinterpret_cast<const float4 *>(cq);
+        Bv[0] = make_float2(b4.x, b4.y);
+        Bv[S / 2 - 1] = make_float2(b4.z, b4.w);
+        Cv[0] = make_float2(c4.x, c4.y);
+        Cv[S / 2 - 1] = make_float2(c4.z, c4.w);
+    } else {
+#pragma unroll
+        for (int p = 0; p < S / 2; ++p) {
+            Bv[p] = reinterpret_cast<const float2 *>(bq)[p];
+            Cv[p] = reinterpret_cast<const float2 *>(cq)[p];
+        }
+    }
+    const float2 dt2 = make_float2(dt, dt), x2 = make_float2(x, x);
+    float2 y = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < S / 2; ++p) {
+        const float2 dA = __fmul2_rn(dt2, ac[p]);
+        const float2 a = make_float2(ex2_approx(dA.x), ex2_approx(dA.y));
+        const float2 w = __fmul2_rn(x2, Bv[p]);
+        if (SMALLA) {
+            h[p].x = state_update(a.x, w.x, kI[p].x, dt, h[p].x);
+            h[p].y = state_update(a.y, w.y, kI[p].y, dt, h[p].y);
+        } else {
+            const float2 sk = __ffma2_rn(w, kI[p], h[p]);
+            h[p] = __ffma2_rn(__fadd2_rn(a, make_float2(-1.f, -1.f)), sk, h[p]);
+        }
+        y = __ffma2_rn(Cv[p], h[p], y);
+    }
+    return y.x + y.y;
+}
+
+template <int NS, int TT, int ST, typename Tx, typename Tdt, typename Tbc>
+__global__ void __launch_bounds__(128, 4)
+    scan_quad_kernel(const ScanKParams p, const __grid_constant__ CUtensorMap tmx,
+                     const __grid_constant__ CUtensorMap tmdt, const __grid_constant__ CUtensorMap tmz,
+                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC) {
+    constexpr int S = NS / 4, CPB = kQuadCPB;
+    using Lay = TmaLayout<NS, CPB, TT, ST, Tx, Tdt, Tbc>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);                    // [2][TT][2*NS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ST * Lay::kStage + Lay::kBC);  // [ST]
+
+    const int tid = threadIdx.x, q = tid & 3, c = tid >> 2, qbase = (tid & 31) & ~3;
+    const int b = blockIdx.y;
+    const int d0 = blockIdx.x * CPB, d = d0 + c;
+    const bool valid = d < p.D;
+    const int dd = valid ? d : 0;
+    const int N = p.N, L = p.L;
+    const int ntiles = (L + TT - 1) / TT;
+    const bool has_z = p.z != nullptr;
+    const uint32_t bc_box = (uint32_t)(N * TT * (int)sizeof(Tbc));
+    const uint32_t tx_bytes = Lay::kXB + Lay::kDB + (has_z ? Lay::kXB : 0) + 2u * bc_box;
+
+    static_assert(S % 2 == 0, "4 lanes x an even number of states");
+    float2 ac[S / 2], kI[S / 2], h[S / 2];
+    bool small = false;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        const int n = q * S + j;
+        const float a = (valid && n < N) ? p.A[(int64_t)dd * N + n] : 0.f;
+        const float ki = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
+        const float h0 = (valid && n < N && p.h_init) ? p.h_init[((int64_t)b * p.D + dd) * N + n] : 0.f;
+        small |= ki == 0.f;
+        if (j & 1) {
+            ac[j / 2].y = a * kLog2e;
+            kI[j / 2].y = ki;
+            h[j / 2].y = h0;
+        } else {
+            ac[j / 2].x = a * kLog2e;
+            kI[j / 2].x = ki;
+            h[j / 2].x = h0;
+        }
+    }
+    const bool has_bias = p.dt_bias != nullptr;
+    const float bias = (has_bias && valid) ? p.dt_bias[dd] : 0.f;
+    const float dskip = (p.Dskip && valid) ? p.Dskip[dd] : 0.f;
+    Tx *gy = static_cast<Tx *>(p.y) + (int64_t)b * p.sy[0] + (int64_t)dd * p.sy[2];
+
+    if (tid == 0) {
+        prefetch_tensormap(&tmx);
+        prefetch_tensormap(&tmdt);
+        if (has_z) prefetch_tensormap(&tmz);
+        prefetch_tensormap(&tmB);
+        prefetch_tensormap(&tmC);
+        for (int s = 0; s < ST; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    // A state with |A| <= 1e-6 anywhere in the CTA selects the per-state
+    // branch of the update (uniform, so the packed form serves the rest).
+    const bool any_small = __syncthreads_or(small);
+
+    auto issue = [&](int tile, int s) {
+        unsigned char *stg = smem + s * Lay::kStage;
+        const int t = tile * TT;
+        mbar_arrive_expect_tx(&bars[s], tx_bytes);
+        tma_load_3d(stg, &tmx, &bars[s], d0, t, b);
+        tma_load_3d(stg + Lay::kOffD, &tmdt, &bars[s], d0, t, b);
+        if (has_z) tma_load_3d(stg + Lay::kOffZ, &tmz, &bars[s], d0, t, b);
+        tma_load_3d(stg + Lay::kOffB, &tmB, &bars[s], 0, t, b);
+        tma_load_3d(stg + Lay::kOffC, &tmC, &bars[s], 0, t, b);
+    };
+    auto stage_bc = [&](int s, int t0, float *dst) {
+        const unsigned char *stg = smem + s * Lay::kStage;
+        convert_bc<NS, 128, TT, Tbc, false>(reinterpret_cast<const Tbc *>(stg + Lay::kOffB),
+                                            reinterpret_cast<const Tbc *>(stg + Lay::kOffC), dst, N, t0, L);
+    };
+    if (tid == 0)
+        for (int s = 0; s < min(ST, ntiles); ++s) issue(s, s);
+
+    bool ok0 = true;
+    if (ntiles > 0) {
+        ok0 = mbar_wait_bounded(&bars[0], 0u);
+        if (ok0) stage_bc(0, 0, bcf);
+    }
+    int i = 0;
+    bool aborted = __syncthreads_or(!ok0);
+    for (; !aborted && i < ntiles; ++i) {
+        const int s = i % ST;
+        const int t0 = i * TT;
+        const int nt = min(TT, L - t0);
+        // warp-uniform verdict: the shuffles below need every lane
+        bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], (uint32_t)((i / ST) & 1)));
+        if (ok) {
+            const unsigned char *stg = smem + s * Lay::kStage;
+            const Tx *sX = reinterpret_cast<const Tx *>(stg);
+            const Tdt *sDt = reinterpret_cast<const Tdt *>(stg + Lay::kOffD);
+            const Tx *sZ = reinterpret_cast<const Tx *>(stg + Lay::kOffZ);
+            const float *sBC = bcf + (i & 1) * TT * 2 * NS;
+            // Groups of four timesteps: lane q evaluates x, softplus(delta)
+            // and SiLU(z) of timestep q of the group (one each, so the quad
+            // does no redundant special-function work) and the quad shares
+            // them by shuffle; then the four recurrences, whose C*h sums are
+            // reduced after the group, off the state's dependency chain.
+            auto group = [&](const int g0, const int lim, auto small_tag) {
+                constexpr bool SMALLA = decltype(small_tag)::value;
+                const int sq = g0 + q;  // < TT: TT is a multiple of 4
+                const float xq = cvt_f32(sX[sq * CPB + c]);
+                float drq = cvt_f32(sDt[sq * CPB + c]);
+                if (has_bias) drq = __fadd_rn(drq, bias);
+                const float dq = softplus_fast(drq);
+                const float gq = has_z ? silu_fast(cvt_f32(sZ[sq * CPB + c])) : 1.f;
+                float xs[4], ds[4], gs[4], yp[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    xs[k] = __shfl_sync(0xffffffffu, xq, qbase | k);
+                    ds[k] = __shfl_sync(0xffffffffu, dq, qbase | k);
+                    gs[k] = __shfl_sync(0xffffffffu, gq, qbase | k);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    yp[k] = 0.f;
+                    if (g0 + k < lim) {  // uniform across the CTA
+                        const float *bc = sBC + (g0 + k) * 2 * NS + q * S;
+                        yp[k] = quad_states<S, SMALLA>(xs[k], ds[k], bc, bc + NS, h, ac, kI);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    yp[k] += __shfl_xor_sync(0xffffffffu, yp[k], 1);
+                    yp[k] += __shfl_xor_sync(0xffffffffu, yp[k], 2);
+                }
+                // lane k of the quad stores timestep k of the group
+                float yo = yp[0], xo = xs[0], go = gs[0];
+#pragma unroll
+                for (int k = 1; k < 4; ++k)
+                    if (q == k) {
+                        yo = yp[k];
+                        xo = xs[k];
+                        go = gs[k];
+                    }
+                if (valid && g0 + q < lim) gy[(int64_t)(t0 + g0 + q) * p.sy[1]] = cvt_out<Tx>(fmaf(dskip, xo, yo) * go);
+            };
+            using Small = std::integral_constant<bool, true>;
+            using Packed = std::integral_constant<bool, false>;
+            if (nt == TT && !any_small) {
+                // full tile: every offset and bound is a compile-time constant
+#pragma unroll
+                for (int g0 = 0; g0 < TT; g0 += 4) group(g0, TT, Packed{});
+            } else if (any_small) {
+                for (int g0 = 0; g0 < nt; g0 += 4) group(g0, nt, Small{});
+            } else {
+                for (int g0 = 0; g0 < nt; g0 += 4) group(g0, nt, Packed{});
+            }
+        }
+        if (i + 1 < ntiles) {
+            float *next = bcf + ((i + 1) & 1) * TT * 2 * NS;
+            const int s1 = (i + 1) % ST;
+            const bool ok1 = mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1));
+            if (ok1) stage_bc(s1, t0 + TT, next);
+            ok = ok && ok1;
+        }
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            break;
+        }
+        if (tid == 0 && i + ST < ntiles) issue(i + ST, s);
+    }
+    if (aborted) {
+        if (tid == 0) {
+            atomicOr(&g_device_error, kErrTmaTimeout);
+            for (int j = i; j < min(i + ST, ntiles); ++j)
+                mbar_wait_bounded(&bars[j % ST], (uint32_t)((j / ST) & 1));
+        }
+        __syncthreads();
+        return;
+    }
+    if (p.final_state && valid) {
+#pragma unroll
+        for (int j = 0; j < S; ++j)
+            if (q * S + j < N)
+                p.final_state[((int64_t)b * p.D + d) * N + q * S + j] = (j & 1) ? h[j / 2].y : h[j / 2].x;
+    }
+}
+
 // ---- phase 2 and the cross-rank composition -----------------------------------
 // Compose the chunk summaries of every (b, d, n) in time order.  On entry
 // H/P hold the summaries [batch, nchunks, D*N]; when write_hin is set, H is
@@ -695,8 +932,73 @@ int launch_combine(const float *P, float *H, const float *h0, int nchunks, int64
 
 }  // namespace
 
+namespace {
+
+// The four-lanes-per-channel pass serves FP16 problems that would otherwise
+// be split into time chunks (fewer 128-channel CTAs than SMs) but have at
+// least one 32-channel CTA per SM, in the layout its TMA tiles need
+// (channel-contiguous rows, 16-byte aligned; B and C with exactly 8 or 16
+// states).  Other problems keep the chunked path.
+bool quad_rows_ok(const void *ptr, const int64_t *st, int es, int dim0, int batch) {
+    if (!ptr) return true;  // not given: checked where it is required
+    if (st[2] != 1 || reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    const int64_t row = st[1] * es, bat = st[0] * es;
+    return row > 0 && row % 16 == 0 && row >= (int64_t)dim0 * es && (batch == 1 || (bat > 0 && bat % 16 == 0));
+}
+
+bool use_quad(const MambaScanArgs *a) {
+    if (a->chunk_len > 0 || a->seqlen <= 0 || a->x_dtype != MAMBA_F16) return false;
+    if (a->dstate != 8 && a->dstate != 16) return false;
+    const int sms = device_sm_count();
+    const int64_t ctas = (int64_t)a->batch * ceil_div(a->dim, kScanCH);
+    const int64_t quads = (int64_t)a->batch * ceil_div(a->dim, kQuadCPB);
+    if (ctas >= sms || quads < sms) return false;
+    const int xs = 2, ds = a->delta_dtype == MAMBA_F16 ? 2 : 4, bs = a->bc_dtype == MAMBA_F16 ? 2 : 4;
+    return quad_rows_ok(a->x, a->x_stride, xs, a->dim, a->batch) &&
+           quad_rows_ok(a->delta, a->delta_stride, ds, a->dim, a->batch) &&
+           quad_rows_ok(a->z, a->z_stride, xs, a->dim, a->batch) &&
+           quad_rows_ok(a->B, a->B_stride, bs, a->dstate, a->batch) &&
+           quad_rows_ok(a->C, a->C_stride, bs, a->dstate, a->batch);
+}
+
+template <int NS, typename Tdt, typename Tbc>
+int launch_quad_t(const ScanKParams &kp, int dd, int bd, cudaStream_t st) {
+    constexpr int TT = kTmaTT, ST = kTmaStages;
+    CUtensorMap maps[5];
+    const bool ok = encode_map(&maps[0], kp.x, MAMBA_F16, kp.D, kp.L, kp.batch, kp.sx, kQuadCPB) &&
+                    encode_map(&maps[1], kp.delta, dd, kp.D, kp.L, kp.batch, kp.sdt, kQuadCPB) &&
+                    (!kp.z || encode_map(&maps[2], kp.z, MAMBA_F16, kp.D, kp.L, kp.batch, kp.sz, kQuadCPB)) &&
+                    encode_map(&maps[3], kp.B, bd, kp.N, kp.L, kp.batch, kp.sB, kp.N) &&
+                    encode_map(&maps[4], kp.C, bd, kp.N, kp.L, kp.batch, kp.sC, kp.N);
+    MB_CHECK_ARG(ok, "selective_scan: tensor map encoding failed");
+    if (!kp.z) maps[2] = maps[0];  // unused by the kernel
+    auto kern = scan_quad_kernel<NS, TT, ST, __half, Tdt, Tbc>;
+    const int smem = TmaLayout<NS, kQuadCPB, TT, ST, __half, Tdt, Tbc>::kBytes;
+    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dim3 grid(ceil_div(kp.D, kQuadCPB), kp.batch);
+    kern<<<grid, 128, smem, st>>>(kp, maps[0], maps[1], maps[2], maps[3], maps[4]);
+    return launch_status("selective scan (4 lanes per channel) kernel");
+}
+
+template <int NS>
+int launch_quad_ns(const ScanKParams &kp, int dd, int bd, cudaStream_t st) {
+    if (dd == MAMBA_F16 && bd == MAMBA_F16) return launch_quad_t<NS, __half, __half>(kp, dd, bd, st);
+    if (dd == MAMBA_F32 && bd == MAMBA_F16) return launch_quad_t<NS, float, __half>(kp, dd, bd, st);
+    if (dd == MAMBA_F32 && bd == MAMBA_F32) return launch_quad_t<NS, float, float>(kp, dd, bd, st);
+    set_error("selective_scan: unsupported dtype combination (x, delta, B/C)");
+    return -1;
+}
+
+int launch_quad(const ScanKParams &kp, const MambaScanArgs *a, cudaStream_t st) {
+    if (a->dstate == 8) return launch_quad_ns<8>(kp, a->delta_dtype, a->bc_dtype, st);
+    return launch_quad_ns<16>(kp, a->delta_dtype, a->bc_dtype, st);
+}
+
+}  // namespace
+
 size_t scan_workspace_bytes(const MambaScanArgs *a) {
     if (!a || a->batch <= 0 || a->dim <= 0 || a->seqlen <= 0) return 0;
+    if (use_quad(a)) return 0;
     const int clen = choose_chunk_len(a->batch, a->seqlen, a->dim, a->chunk_len);
     const int nc = ceil_div(a->seqlen, clen);
     if (nc <= 1) return 0;
@@ -707,6 +1009,11 @@ int selective_scan(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream
     if (validate(a)) return -1;
     if (a->batch == 0 || a->dim == 0) return 0;
     if (a->seqlen > 0) MB_CHECK_ARG(a->y && a->C, "selective_scan: y and C are required");
+    if (use_quad(a)) {
+        ScanKParams kp = make_params(a, a->seqlen);
+        kp.h_init = a->initial_state;
+        return launch_quad(kp, a, st);
+    }
     const int clen = choose_chunk_len(a->batch, a->seqlen, a->dim, a->chunk_len);
     ScanKParams kp = make_params(a, clen);
     const int64_t DN = (int64_t)a->dim * a->dstate;

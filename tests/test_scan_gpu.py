@@ -229,3 +229,45 @@ def test_workspace_too_small_is_an_error(cuda):
     assert need > 0
     assert mb.lib().mamba_selective_scan(ctypes.byref(a), None, 0, None) == -1
     assert "workspace" in mb.last_error()
+
+
+QUAD_CASES = [
+    # (N, delta dtype, B/C dtype, time_major)
+    (16, torch.float16, torch.float16, True),    # vector B/C loads
+    (16, torch.float32, torch.float32, True),
+    (8, torch.float16, torch.float16, True),     # fewer states per lane
+    (4, torch.float32, torch.float32, True),     # one state per lane: chunked path instead
+    (5, torch.float32, torch.float16, True),     # not 4/8/16 states: chunked path instead
+    (16, torch.float16, torch.float16, False),   # [B, D, L] storage: chunked path instead
+]
+
+
+@pytest.mark.parametrize("N,tdt,tbc,time_major", QUAD_CASES)
+def test_four_lanes_per_channel_pass(cuda, N, tdt, tbc, time_major):
+    """Batch 5 x 1024 channels: fewer 128-channel CTAs than SMs but enough
+    32-channel ones, so the single pass with four lanes per channel runs (no
+    workspace) where its TMA layout holds; gated output, dt bias, initial and
+    final state vs the oracle, over a length that is not a multiple of the
+    16-step tiles."""
+    bsz, L, D = 5, 301, 1024
+    x, dr, B, C, z, A, Dk = scan_inputs(31, bsz, L, D, N)
+    rng = np.random.default_rng(8)
+    bias = rng.normal(0, 0.5, D).astype(np.float32)
+    h0 = (rng.standard_normal((bsz, D, N)) * 0.3).astype(np.float32)
+    x, z = r16(x), r16(z)
+    if tdt == torch.float16:
+        dr = r16(dr)
+    if tbc == torch.float16:
+        B, C = r16(B), r16(C)
+    tx, tdr = dev(x, torch.float16, time_major), dev(dr, tdt, time_major)
+    tB, tC, tz = dev(B, tbc, time_major), dev(C, tbc, time_major), dev(z, torch.float16, time_major)
+    bc_row_bytes = N * (2 if tbc == torch.float16 else 4)
+    quad = N in (8, 16) and time_major and bc_row_bytes % 16 == 0
+    assert (mb.scan_workspace_bytes(tx, tdr, dev(A), tB) == 0) == quad
+    y_ref, h_ref = oracle.scan(x, dr, B, C, A, Dk, z=z, dt_bias=bias, h0=h0)
+    y, h = mb.selective_scan(tx, tdr, dev(A), tB, tC, D=dev(Dk), z=tz, dt_bias=dev(bias),
+                             initial_state=dev(h0), return_final_state=True)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    assert err(y, y_ref) < TOL16
+    assert err(h, h_ref) < TOL32
