@@ -210,8 +210,13 @@ struct Model {
 
     ~Model() {
         if (stream) cudaStreamSynchronize(stream);
+        if (h2d) cudaStreamSynchronize(h2d);
+        if (d2h) cudaStreamSynchronize(d2h);
         step_graph.reset();
         if (cublas) cublasDestroy(cublas);
+        for (cudaEvent_t e : io_events) cudaEventDestroy(e);
+        if (h2d) cudaStreamDestroy(h2d);
+        if (d2h) cudaStreamDestroy(d2h);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -250,6 +255,7 @@ struct Model {
         MB_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
         if (const char *g = std::getenv("MAMBA_STEP_GRAPH")) use_graphs = std::atoi(g) != 0;
         if (const char *t = std::getenv("MAMBA_TC_LINEAR")) tc_linear = std::atoi(t) != 0;
+        if (const char *h = std::getenv("MAMBA_HOST_CHUNKS")) host_chunks = std::max(0, std::atoi(h));
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -466,6 +472,15 @@ struct Model {
         return 0;
     }
 
+    // Host-buffer forward.  Large inputs are cut into row chunks: chunk k+1
+    // is uploaded and chunk k-1 downloaded on copy streams while chunk k is
+    // computed, so the PCIe transfers hide behind the layers (overlap needs
+    // pinned host memory; pageable buffers are staged by the driver).
+    static constexpr size_t kChunkedHostBytes = 64u << 20;
+    int host_chunks = 0;  // MAMBA_HOST_CHUNKS: forced chunk count (0 = automatic)
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    std::vector<cudaEvent_t> io_events;
+
     int forward_host(const float *in, float *out, int batch, int L) {
         MB_CHECK_ARG(batch >= 0 && L >= 0, "forward: negative batch or seq_len");
         const int64_t T = (int64_t)batch * L;
@@ -476,10 +491,54 @@ struct Model {
         MB_CUDA_TRY(cudaStreamSynchronize(st));
         if (io.reserve(bytes)) return -1;
         float *d = static_cast<float *>(io.ptr);
-        MB_CUDA_TRY(cudaMemcpyAsync(d, in, bytes, cudaMemcpyHostToDevice, st));
-        if (forward_device(d, d, batch, L, st)) return -1;
-        MB_CUDA_TRY(cudaMemcpyAsync(out, d, bytes, cudaMemcpyDeviceToHost, st));
-        MB_CUDA_TRY(cudaStreamSynchronize(st));
+        int chunks = host_chunks > 0 ? host_chunks : (bytes >= kChunkedHostBytes ? 2 : 1);
+        chunks = std::max(1, std::min(chunks, batch));
+        if (chunks == 1) {
+            MB_CUDA_TRY(cudaMemcpyAsync(d, in, bytes, cudaMemcpyHostToDevice, st));
+            if (forward_device(d, d, batch, L, st)) return -1;
+            MB_CUDA_TRY(cudaMemcpyAsync(out, d, bytes, cudaMemcpyDeviceToHost, st));
+            MB_CUDA_TRY(cudaStreamSynchronize(st));
+            return 0;
+        }
+        if (!h2d) MB_CUDA_TRY(cudaStreamCreateWithFlags(&h2d, cudaStreamNonBlocking));
+        if (!d2h) MB_CUDA_TRY(cudaStreamCreateWithFlags(&d2h, cudaStreamNonBlocking));
+        while ((int)io_events.size() < 2 * chunks) {
+            cudaEvent_t e;
+            MB_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            io_events.push_back(e);
+        }
+        const int rows = (batch + chunks - 1) / chunks;
+        const size_t row_elems = (size_t)L * M;
+        int err = 0;
+        for (int k = 0; k < chunks; ++k) {
+            const int r0 = k * rows, nr = std::min(rows, batch - r0);
+            if (nr <= 0) break;
+            MB_CUDA_TRY(cudaMemcpyAsync(d + r0 * row_elems, in + r0 * row_elems, sizeof(float) * nr * row_elems,
+                                        cudaMemcpyHostToDevice, h2d));
+            MB_CUDA_TRY(cudaEventRecord(io_events[2 * k], h2d));
+        }
+        for (int k = 0; k < chunks && !err; ++k) {
+            const int r0 = k * rows, nr = std::min(rows, batch - r0);
+            if (nr <= 0) break;
+            float *dk = d + r0 * row_elems;
+            MB_CUDA_TRY(cudaStreamWaitEvent(st, io_events[2 * k], 0));
+            if (forward_device(dk, dk, nr, L, st)) {
+                err = -1;
+                break;
+            }
+            MB_CUDA_TRY(cudaEventRecord(io_events[2 * k + 1], st));
+            MB_CUDA_TRY(cudaStreamWaitEvent(d2h, io_events[2 * k + 1], 0));
+            MB_CUDA_TRY(cudaMemcpyAsync(out + r0 * row_elems, dk, sizeof(float) * nr * row_elems,
+                                        cudaMemcpyDeviceToHost, d2h));
+        }
+        // every queued copy and kernel finishes before returning, error or not
+        const cudaError_t e1 = cudaStreamSynchronize(h2d);
+        const cudaError_t e2 = cudaStreamSynchronize(st);
+        const cudaError_t e3 = cudaStreamSynchronize(d2h);
+        if (err) return -1;
+        MB_CUDA_TRY(e1);
+        MB_CUDA_TRY(e2);
+        MB_CUDA_TRY(e3);
         return 0;
     }
 };

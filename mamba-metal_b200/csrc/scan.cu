@@ -538,9 +538,9 @@ __global__ void __launch_bounds__(128, 4)
     for (int j = 0; j < S; ++j) {
         const int n = q * S + j;
         const float a = (valid && n < N) ? p.A[(int64_t)dd * N + n] : 0.f;
-        const float ki = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
+        const float ki = fabsf(a) > 1e-6f ? __frcp_rn(a) : 0.f;
         const float h0 = (valid && n < N && p.h_init) ? p.h_init[((int64_t)b * p.D + dd) * N + n] : 0.f;
-        small |= ki == 0.f;
+        small |= valid && n < N && ki == 0.f;
         if (j & 1) {
             ac[j / 2].y = a * kLog2e;
             kI[j / 2].y = ki;

@@ -108,7 +108,7 @@ __device__ __forceinline__ bool load_channel_consts(const float *__restrict__ A,
             a[q] = (valid && n < N) ? A[row * N + n] : 0.f;
             c[q] = PRECISE ? a[q] : a[q] * kLog2e;
             const bool big = fabsf(a[q]) > 1e-6f;
-            k[q] = big ? 1.0f / a[q] : 0.f;
+            k[q] = big ? __frcp_rn(a[q]) : 0.f;  // correctly rounded, as 1.0f / a
             small |= (valid && n < N && !big);
         }
         Ac[p] = make_float2(c[0], c[1]);

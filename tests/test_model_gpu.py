@@ -209,3 +209,27 @@ def test_decode_with_tcgen05_projections_matches_cublas(cuda, monkeypatch):
     h = rng.standard_normal((2, 50, 256)).astype(np.float32)
     assert oracle.normwise_rel_err(tc.forward(h) - h, ref.forward(h) - h) < 2e-3
     assert mb.device_status() == 0
+
+
+def test_chunked_host_forward_matches_device_forward(cuda, monkeypatch):
+    """mamba_forward with the batch cut into row chunks (uploads, compute and
+    downloads overlapped on separate streams) gives the rows of the
+    single-call device forward (per-row results may take other kernel paths
+    at the smaller batch, so within the FP16 tolerance)."""
+    rng = np.random.default_rng(109)
+    cfg = mb.MambaConfig(128, 16, 4, 2, 2, mb.F16)
+    layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
+    blob = mb.make_weight_blob(cfg, layers)
+    monkeypatch.setenv("MAMBA_HOST_CHUNKS", "3")
+    m = mb.Model(128, 16, 4, 2, 2, mb.F16)
+    m.load_weights(blob)
+    h = rng.standard_normal((7, 200, 128)).astype(np.float32)
+    out = m.forward(h)  # 3 chunks of 3, 3 and 1 rows
+    dh = torch.from_numpy(h).cuda()
+    dout = torch.empty_like(dh)
+    m.forward_device(dh.data_ptr(), dout.data_ptr(), 7, 200)
+    torch.cuda.synchronize()
+    ref = dout.cpu().numpy()
+    assert oracle.normwise_rel_err(out - h, ref - h) < 2e-3
+    ref_cpu = block_ref.model_forward(h, layers, cfg, block_ref.F16)
+    assert oracle.normwise_rel_err(out - h, ref_cpu - h) < 2e-3
