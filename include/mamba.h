@@ -102,9 +102,17 @@ const char *mamba_last_error(void);
  * selective scan exceeded its 2-second bound, so that call stopped early and
  * its outputs are invalid.  Bit 1: the same for a wait inside
  * mamba_gated_mlp_up.  Bit 2: the same for mamba_linear (and the decode
- * projections that use it).  Waits for the device; clear != 0 resets
- * them. */
+ * projections that use it).  Bit 3: set by mamba_selftest_bounded_wait.
+ * Waits for the device; clear != 0 resets them. */
 unsigned mamba_device_status(int clear);
+
+/* Health check of the device-side failure path: launches one thread that
+ * waits, through the same bounded mbarrier wait the kernels use, on a
+ * barrier nothing completes, with a limit of limit_us microseconds
+ * (1..1000000).  Returns 0 when the wait gave up on time and reported it
+ * (bit 3 of mamba_device_status is then set; the context stays usable),
+ * -1 otherwise. */
+int mamba_selftest_bounded_wait(unsigned limit_us, void *stream);
 
 /* dt_rank used for a config: ceil(d_model / 16). */
 int mamba_dt_rank(const MambaConfig *cfg);

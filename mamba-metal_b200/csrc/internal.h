@@ -18,6 +18,7 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
 int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
                         float *h_in, cudaStream_t st);
 unsigned device_error_flags(bool clear);
+int bounded_wait_selftest(unsigned limit_us, cudaStream_t st);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st);
 

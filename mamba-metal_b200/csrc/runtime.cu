@@ -957,6 +957,11 @@ unsigned mamba_device_status(int clear) {
     return (scan == ~0u || gemm == ~0u || lin == ~0u) ? ~0u : (scan | gemm | lin);
 }
 
+int mamba_selftest_bounded_wait(unsigned limit_us, void *stream) {
+    mb::clear_error();
+    return mb::bounded_wait_selftest(limit_us, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
 int mamba_dt_rank(const MambaConfig *cfg) { return cfg ? (cfg->d_model + 15) / 16 : -1; }
 
 size_t mamba_weights_blob_size(const MambaConfig *cfg) {

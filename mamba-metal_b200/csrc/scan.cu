@@ -1118,6 +1118,41 @@ int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st) {
     return selective_scan(a, ws, need > 0 ? kNoAllocScratchBytes : 0, st);
 }
 
+namespace {
+
+// A bounded mbarrier wait that nothing completes: the CTA's one thread
+// initialises a barrier expecting one arrival, makes none, waits with the
+// given limit through the same helper the pipelines use, and on timeout
+// records kErrWaitSelftest in the device status and returns.
+constexpr unsigned kErrWaitSelftest = 8u;
+
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, int *waited_out) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const bool ok = mbar_wait_bounded(&bar, 0u, limit_ns);
+    *waited_out = ok ? 0 : 1;
+    if (!ok) atomicOr(&g_device_error, kErrWaitSelftest);
+}
+
+}  // namespace
+
+int bounded_wait_selftest(unsigned limit_us, cudaStream_t st) {
+    MB_CHECK_ARG(limit_us > 0 && limit_us <= 1000000u, "bounded_wait_selftest: limit must be in (0, 1 s]");
+    int *flag = nullptr;
+    MB_CUDA_TRY(cudaMallocAsync(&flag, sizeof(int), st));
+    MB_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int), st));
+    bounded_wait_selftest_kernel<<<1, 32, 0, st>>>((uint64_t)limit_us * 1000ull, flag);
+    if (launch_status("bounded-wait selftest kernel")) return -1;
+    int h = 0;
+    MB_CUDA_TRY(cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MB_CUDA_TRY(cudaFreeAsync(flag, st));
+    MB_CUDA_TRY(cudaStreamSynchronize(st));
+    MB_CHECK_ARG(h == 1, "bounded_wait_selftest: the wait did not report a timeout");
+    return 0;
+}
+
 unsigned device_error_flags(bool clear) {
     unsigned v = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return ~0u;

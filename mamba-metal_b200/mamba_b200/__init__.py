@@ -114,6 +114,7 @@ _PROTOTYPES = {
     "mamba_gated_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_void_p]),
     "mamba_gated_mlp_up": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int, c_void_p]),
     "mamba_linear_workspace": (c_size, [c_i64, c_int, c_int]),
+    "mamba_selftest_bounded_wait": (c_int, [ctypes.c_uint, c_void_p]),
     "mamba_linear": (c_int, [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_int, c_int, c_int,
                              c_void_p, c_size, c_void_p]),
 }

@@ -110,3 +110,51 @@ def test_sequence_parallel_scan_gloo(world, L):
     y = np.concatenate([results[r][0] for r in range(world)], axis=1)
     assert oracle.normwise_rel_err(y, y_ref) < 1e-5
     assert oracle.normwise_rel_err(results[world - 1][1], h_ref) < 1e-5
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 leaves before the carry exchange (between steps, nothing in
+    flight); rank 0 must come back with an error from its collective within
+    the short process-group timeout instead of waiting forever."""
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "mamba-metal_b200")):
+        sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    def report(msg):
+        q.put((rank, msg))
+        q.close()
+        q.join_thread()  # the message is out before the process ends
+
+    if rank == 1:
+        report("left")
+        os._exit(0)  # leaves without taking part in the exchange
+    from mamba_b200.seqpar import sequence_parallel_scan
+    x, dr, B, C, z, A, Dk, bias, h0 = _inputs(32)
+    t = torch.from_numpy
+    t0 = time.monotonic()
+    try:
+        sequence_parallel_scan(t(np.ascontiguousarray(x[:, :16])), t(np.ascontiguousarray(dr[:, :16])), t(A),
+                               t(np.ascontiguousarray(B[:, :16])), t(np.ascontiguousarray(C[:, :16])), D=t(Dk),
+                               z=t(np.ascontiguousarray(z[:, :16])), dt_bias=t(bias), h0=t(h0), ops=OracleOps)
+        report("returned")
+    except Exception as e:  # the collective reports the missing peer
+        report("error after %.1f s: %s" % (time.monotonic() - t0, type(e).__name__))
+    os._exit(0)
+
+
+def test_missing_rank_is_reported_not_hung():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=60) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1] == "left"
+    assert got[0].startswith("error after"), got[0]
