@@ -1,6 +1,7 @@
 // norm.cu -- RMSNorm (Sources/Kernels/rmsnorm.metal:11-81):
 //   y = x * rsqrt(mean(x^2) + eps) * w
-// One warp per row: the row is read once into registers (up to
+// One warp per row (one CTA per row when there are few rows): the row is
+// read once into registers (up to
 // kRowRegs * 32 * 4 elements; longer rows re-read from L2), squared and
 // summed in FP32 with a butterfly reduction, then scaled and written in the
 // output type.  HBM-bound: reads 4 or 2 bytes and writes 2 or 4 bytes per
@@ -116,6 +117,72 @@ __global__ void rmsnorm_kernel(const Tin *__restrict__ x, const float *__restric
     }
 }
 
+// Few rows (decode batches): one CTA per row, so a row's loads are spread
+// over 256 threads instead of one warp and the grid still covers the SMs.
+// Each thread caches up to kBlockRegs float4 chunks; longer rows re-read.
+constexpr int kBlockThreads = 256;
+constexpr int kBlockRegs = 4;
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kBlockThreads)
+    rmsnorm_row_block_kernel(const Tin *__restrict__ x, const float *__restrict__ w, Tout *__restrict__ y,
+                             int cols, float eps) {
+    __shared__ float partial[kBlockThreads / 32];
+    const int64_t row = blockIdx.x;
+    const Tin *xr = x + row * cols;
+    Tout *yr = y + row * cols;
+    const int nvec = cols >> 2;
+    float4 cache[kBlockRegs];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kBlockRegs; ++i) {
+        const int v = threadIdx.x + i * kBlockThreads;
+        if (v < nvec) {
+            cache[i] = Vec4<Tin>::load(xr + 4 * v);
+            ss = fmaf(cache[i].x, cache[i].x, ss);
+            ss = fmaf(cache[i].y, cache[i].y, ss);
+            ss = fmaf(cache[i].z, cache[i].z, ss);
+            ss = fmaf(cache[i].w, cache[i].w, ss);
+        }
+    }
+    for (int v = threadIdx.x + kBlockRegs * kBlockThreads; v < nvec; v += kBlockThreads) {
+        const float4 c = Vec4<Tin>::load(xr + 4 * v);
+        ss = fmaf(c.x, c.x, ss);
+        ss = fmaf(c.y, c.y, ss);
+        ss = fmaf(c.z, c.z, ss);
+        ss = fmaf(c.w, c.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kBlockThreads / 32; ++i) tot += partial[i];
+    const float inv = rsqrtf(tot / (float)cols + eps);
+    auto emit = [&](int v, float4 c) {
+        c.x *= inv;
+        c.y *= inv;
+        c.z *= inv;
+        c.w *= inv;
+        if (w) {
+            const float4 g = *reinterpret_cast<const float4 *>(w + 4 * v);
+            c.x *= g.x;
+            c.y *= g.y;
+            c.z *= g.z;
+            c.w *= g.w;
+        }
+        store4<Tout>(yr + 4 * v, c);
+    };
+#pragma unroll
+    for (int i = 0; i < kBlockRegs; ++i) {
+        const int v = threadIdx.x + i * kBlockThreads;
+        if (v < nvec) emit(v, cache[i]);
+    }
+    for (int v = threadIdx.x + kBlockRegs * kBlockThreads; v < nvec; v += kBlockThreads)
+        emit(v, Vec4<Tin>::load(xr + 4 * v));
+}
+
 template <typename Tin, typename Tout>
 int launch_norm(const void *x, const float *w, void *y, int64_t rows, int cols, float eps,
                 cudaStream_t st) {
@@ -127,6 +194,11 @@ int launch_norm(const void *x, const float *w, void *y, int64_t rows, int cols, 
     const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) % 16) == 0) &&
                      ((reinterpret_cast<uintptr_t>(y) % 16) == 0) &&
                      (w == nullptr || (reinterpret_cast<uintptr_t>(w) % 16) == 0);
+    if (vec && rows <= 4LL * device_sm_count()) {
+        rmsnorm_row_block_kernel<Tin, Tout><<<(unsigned)rows, kBlockThreads, 0, st>>>(
+            static_cast<const Tin *>(x), w, static_cast<Tout *>(y), cols, eps);
+        return launch_status("rmsnorm kernel");
+    }
     if (vec)
         rmsnorm_vec_kernel<Tin, Tout><<<(unsigned)blocks, warps * 32, 0, st>>>(
             static_cast<const Tin *>(x), w, static_cast<Tout *>(y), rows, cols, eps);
