@@ -90,7 +90,7 @@ struct ScanKParams {
 // delta, SiLU of the gate) for the whole tile -- independent chains, so the
 // special-function pipe stays busy -- then the state recurrence, whose only
 // serial dependence between timesteps is one packed FMA per state pair.
-template <int NS, int CH, int TT, bool SUMMARY, bool PRECISE, bool SMALLA, typename Tx, typename Tdt>
+template <int NS, int CH, int TT, bool SUMMARY, bool PRECISE, bool SMALLA, bool FULL, typename Tx, typename Tdt>
 __device__ __forceinline__ void run_tile(const ScanKParams &p, int nt, int t0, int b, int d,
                                          const Tx *__restrict__ sX, const Tdt *__restrict__ sDt,
                                          const Tx *__restrict__ sZ, const float *__restrict__ sBC,
@@ -109,7 +109,7 @@ __device__ __forceinline__ void run_tile(const ScanKParams &p, int nt, int t0, i
     Tx *gy = static_cast<Tx *>(p.y) + (int64_t)b * p.sy[0] + (int64_t)t0 * p.sy[1] + (int64_t)d * p.sy[2];
 #pragma unroll
     for (int tt = 0; tt < TT; ++tt) {
-        if (tt < nt) {
+        if (FULL || tt < nt) {
             const float xv = cvt_f32(sX[tt * CH + tid]);
             const float s = scan_step<NS, SUMMARY, PRECISE, SMALLA>(xv, dtv[tt], sBC + tt * 2 * NS, h, Ac, kI, P);
             if (!SUMMARY) gy[(int64_t)tt * p.sy[1]] = cvt_out<Tx>(scan_output<PRECISE>(s, dskip, xv, gv[tt]));
@@ -117,15 +117,26 @@ __device__ __forceinline__ void run_tile(const ScanKParams &p, int nt, int t0, i
     }
 }
 
-// A tile of any length in sub-tiles of SUB timesteps.
-template <int NS, int CH, int SUB, bool SUMMARY, bool PRECISE, bool SMALLA, typename Tx, typename Tdt>
+// A tile of any length in sub-tiles of SUB timesteps; a full tile of TILE
+// timesteps takes a fully unrolled path with every bound known at compile
+// time (no per-step predicates).
+template <int NS, int CH, int SUB, int TILE, bool SUMMARY, bool PRECISE, bool SMALLA, typename Tx, typename Tdt>
 __device__ __forceinline__ void run_steps(const ScanKParams &p, int nt, int t0, int b, int d,
                                           const Tx *__restrict__ sX, const Tdt *__restrict__ sDt,
                                           const Tx *__restrict__ sZ, const float *__restrict__ sBC,
                                           bool has_bias, float bias, float dskip, bool has_z, float2 *h,
                                           const float2 *Ac, const float2 *kI, float2 *P) {
+    static_assert(TILE % SUB == 0, "whole sub-tiles");
+    if (nt == TILE) {
+#pragma unroll
+        for (int s0 = 0; s0 < TILE; s0 += SUB)
+            run_tile<NS, CH, SUB, SUMMARY, PRECISE, SMALLA, true>(
+                p, SUB, t0 + s0, b, d, sX + s0 * CH, sDt + s0 * CH, sZ + s0 * CH, sBC + s0 * 2 * NS, has_bias,
+                bias, dskip, has_z, h, Ac, kI, P);
+        return;
+    }
     for (int s0 = 0; s0 < nt; s0 += SUB)
-        run_tile<NS, CH, SUB, SUMMARY, PRECISE, SMALLA>(
+        run_tile<NS, CH, SUB, SUMMARY, PRECISE, SMALLA, false>(
             p, min(SUB, nt - s0), t0 + s0, b, d, sX + s0 * CH, sDt + s0 * CH, sZ + s0 * CH, sBC + s0 * 2 * NS,
             has_bias, bias, dskip, has_z, h, Ac, kI, P);
 }
@@ -277,10 +288,10 @@ __global__ void __launch_bounds__(CH) scan_generic_kernel(const ScanKParams p) {
         __syncthreads();
         if (dvalid) {
             if (any_small)
-                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, true>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
-                                                           dskip, has_z, h, Ac, kI, P);
+                run_steps<NS, CH, kSubTT, TT, SUMMARY, PRECISE, true>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                                                               bias, dskip, has_z, h, Ac, kI, P);
             else
-                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, false>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
+                run_steps<NS, CH, kSubTT, TT, SUMMARY, PRECISE, false>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias, bias,
                                                             dskip, has_z, h, Ac, kI, P);
         }
         __syncthreads();
@@ -416,10 +427,10 @@ __global__ void __launch_bounds__(CH, kTmaMinCtas)
             const Tx *sZ = reinterpret_cast<const Tx *>(stg + Lay::kOffZ);
             const float *sBC = bcf + (i & 1) * TT * 2 * NS;
             if (any_small)
-                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, true>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                run_steps<NS, CH, kSubTT, TT, SUMMARY, PRECISE, true>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
                                                                    bias, dskip, has_z, h, Ac, kI, P);
             else
-                run_steps<NS, CH, kSubTT, SUMMARY, PRECISE, false>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
+                run_steps<NS, CH, kSubTT, TT, SUMMARY, PRECISE, false>(p, nt, t0, b, d, sX, sDt, sZ, sBC, has_bias,
                                                                     bias, dskip, has_z, h, Ac, kI, P);
         }
         if (i + 1 < ntiles) {
