@@ -271,3 +271,25 @@ def test_four_lanes_per_channel_pass(cuda, N, tdt, tbc, time_major):
     assert mb.device_status() == 0
     assert err(y, y_ref) < TOL16
     assert err(h, h_ref) < TOL32
+
+
+def test_zero_length_and_empty_problems(cuda):
+    """L = 0: no output rows, the final state is the initial state (zero when
+    none is given).  batch 0 or dim 0: nothing to do, no error."""
+    N, D = 16, 64
+    A = dev(np.tile(-np.arange(1, N + 1, dtype=np.float32), (D, 1)))
+    e = torch.empty((2, 0, D), device="cuda")
+    eB = torch.empty((2, 0, N), device="cuda")
+    h0 = torch.randn((2, D, N), device="cuda")
+    y, h = mb.selective_scan(e, e, A, eB, eB, initial_state=h0, return_final_state=True)
+    torch.cuda.synchronize()
+    assert y.shape == (2, 0, D)
+    assert torch.equal(h, h0)
+    _, h = mb.selective_scan(e, e, A, eB, eB, return_final_state=True)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(h) == 0
+    z0 = torch.empty((0, 5, D), device="cuda")
+    y0 = mb.selective_scan(z0, z0, A, torch.empty((0, 5, N), device="cuda"), torch.empty((0, 5, N), device="cuda"))
+    torch.cuda.synchronize()
+    assert y0.shape == (0, 5, D)
+    assert mb.device_status() == 0
