@@ -502,23 +502,35 @@ struct Model {
         }
         if (!h2d) MB_CUDA_TRY(cudaStreamCreateWithFlags(&h2d, cudaStreamNonBlocking));
         if (!d2h) MB_CUDA_TRY(cudaStreamCreateWithFlags(&d2h, cudaStreamNonBlocking));
+        // Row ranges: forced chunk counts split evenly; the automatic split is
+        // [c, batch - 2c, c] with c ~ batch/8, so only the short first upload
+        // and the short last download are exposed.
+        std::vector<int> starts;
+        if (host_chunks > 0 || batch < 3) {
+            const int rows = (batch + chunks - 1) / chunks;
+            for (int r0 = 0; r0 < batch; r0 += rows) starts.push_back(r0);
+        } else {
+            const int c = std::max(1, batch / 8);
+            starts = {0, c, batch - c};
+        }
+        starts.push_back(batch);
+        chunks = (int)starts.size() - 1;
         while ((int)io_events.size() < 2 * chunks) {
             cudaEvent_t e;
             MB_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
             io_events.push_back(e);
         }
-        const int rows = (batch + chunks - 1) / chunks;
         const size_t row_elems = (size_t)L * M;
         int err = 0;
         for (int k = 0; k < chunks; ++k) {
-            const int r0 = k * rows, nr = std::min(rows, batch - r0);
+            const int r0 = starts[k], nr = starts[k + 1] - r0;
             if (nr <= 0) break;
             MB_CUDA_TRY(cudaMemcpyAsync(d + r0 * row_elems, in + r0 * row_elems, sizeof(float) * nr * row_elems,
                                         cudaMemcpyHostToDevice, h2d));
             MB_CUDA_TRY(cudaEventRecord(io_events[2 * k], h2d));
         }
         for (int k = 0; k < chunks && !err; ++k) {
-            const int r0 = k * rows, nr = std::min(rows, batch - r0);
+            const int r0 = starts[k], nr = starts[k + 1] - r0;
             if (nr <= 0) break;
             float *dk = d + r0 * row_elems;
             MB_CUDA_TRY(cudaStreamWaitEvent(st, io_events[2 * k], 0));
