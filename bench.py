@@ -205,6 +205,18 @@ def _cpu_stack(budget_s, use_reference_scan, tokens, seed, oracle, block_ref, mb
     return tps, sample
 
 
+def cpu_block_forward(h, layers, cfg):
+    """The CPU block restatement over every layer on host FP32 input h
+    [1, T, d_model]; returns (output, seconds).  All host threads (torchrun
+    sets OMP_NUM_THREADS=1, so the BLAS pool is resized)."""
+    from oracle import block_ref  # CPU checker, only in this leg
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(limits=os.cpu_count() or 1):
+        t0 = time.perf_counter()
+        ref = block_ref.model_forward(h, layers, cfg, block_ref.F16)
+        return ref, time.perf_counter() - t0
+
+
 def run_reference_arm(args, world, rank):
     """--impl reference: the reference's CPU implementation on this host."""
     if rank != 0:
@@ -353,11 +365,28 @@ def run_stack(args, world, rank, local, C=STACK):
                "h2d_bytes_per_step": b * L * M * 4 * world, "d2h_bytes_per_step": b * L * M * 4 * world,
                "api": "mamba_forward (host FP32, pinned)"}
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and C is STACK:
-        tps, sample = cpu_stack_tokens_per_s(budget_s=args.cpu_budget, use_reference_scan=False)
-        cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": sample}
+    # Parity and the CPU baseline on the same weights: the CPU block
+    # restatement runs all layers over the first `ptok` tokens of the rank's
+    # first row (every op is causal in time, so these outputs of the
+    # full-size GPU forward depend on nothing else) and is timed.
+    cpu = parity = None
+    if rank == 0 and C is STACK and not args.no_parity:
+        ptok = 256
+        cfg = mb.MambaConfig(M, N, C["d_conv"], C["expand"], n_layer, mb.F16)
+        layers = mb.weights_from_blob(cfg, model.save_weights())
+        h = x[:1, :ptok].cpu().numpy()
+        got = out[:1, :ptok].cpu().numpy()
+        ref, dt = cpu_block_forward(h, layers, cfg)
+        err = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref - h)))
+        parity = {"normwise_rel_err": err, "tolerance": 2e-3, "pass": err < 2e-3,
+                  "checked": "row 0, tokens 0..%d, all %d layers, of the timed forward's output, against "
+                             "the CPU block reference on the same weights (mamba_save_weights)" % (ptok - 1, n_layer)}
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = {"value": ptok / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": "1 sequence x %d tokens through all %d layers (CPU block restatement with the "
+                             "oracle scan, numpy BLAS on all host threads), same weights as the GPU run"
+                             % (ptok, n_layer)}
+        del layers
 
     if rank == 0:
         if C is STACK:
@@ -385,6 +414,7 @@ def run_stack(args, world, rank, local, C=STACK):
                              "xu_ceiling": xu},
                 "op_ms_per_layer": breakdown,
                 "gpu_launches": kernels,
+                "parity": parity,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk}
         print(json.dumps(line))
 
@@ -606,6 +636,7 @@ def main():
     ap.add_argument("--seqlen", type=int, default=0, help="override L")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the CPU parity check of the stack output")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

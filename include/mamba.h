@@ -138,6 +138,16 @@ size_t mamba_weights_blob_size(const MambaConfig *cfg);
  * A[d,n] = -(n+1), D = 1, norm_weight = 1.  0 / -1. */
 int mamba_init_weights_random(MambaModel *m, uint64_t seed);
 
+/* Writes the model's weights into a host buffer of exactly
+ * mamba_weights_blob_size(cfg) bytes, in the blob format above, so that
+ * mamba_load_weights on a model of the same config reproduces this model
+ * bit for bit.  Projections come back as the values the GEMMs use (already
+ * rounded to the activation type), widened to FP32.  No counterpart in the
+ * reference, which has no way to read weights back (checkpoint save; also
+ * lets a CPU reference run on the weights of mamba_init_weights_random).
+ * Waits for the model's stream.  0 / -1. */
+int mamba_save_weights(MambaModel *m, void *blob, size_t size);
+
 /* Device-pointer forward: input/output are DEVICE FP32 [batch, seq_len,
  * d_model] on the model's device (may alias).  Enqueued on `stream` (NULL =
  * the model's stream); does not synchronize. */
@@ -244,8 +254,17 @@ int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspa
  * array and nothing in it carries over between calls (every slot a call reads
  * is written earlier by the same call), but calls that overlap on the GPU
  * (other streams, other host threads on the same device) race on it:
- * serialise them.  Results equal mamba_selective_scan's for the same args.
- * 0 / -1. */
+ * serialise them.  When the 32 MiB is committed: with CUDA's default lazy
+ * module loading (CUDA_MODULE_LOADING=LAZY), on a device the first time
+ * this library's scan code is used there -- the first scan call of any
+ * kind, or the first symbol lookup -- not at process start.  A caller that
+ * fixes its device-memory budget at start-up should make one small scan call
+ * (this one, with batch 1 and a short sequence) on each device during
+ * start-up, or run with CUDA_MODULE_LOADING=EAGER so the array is committed
+ * when the library's module is loaded.  A device reset (cudaDeviceReset)
+ * between calls is handled: the address is looked up again in the new
+ * context.  Results equal mamba_selective_scan's, bit for bit, for the same
+ * args.  0 / -1. */
 int mamba_selective_scan_noalloc(const MambaScanArgs *a, void *stream);
 
 /* Sequence-sharded mode, step 1: summary of this rank's slice of the

@@ -6,7 +6,8 @@
 //   transform, so the fill is reproducible and independent of launch shape.
 // * Layout conversion for mamba_load_weights: the blob stores projections
 //   as [K, N] FP32 (x @ W, Sources/Kernels/projection.metal:25-29); the GEMMs
-//   read weights K-major as [N, K] in the activation type.
+//   read weights K-major as [N, K] in the activation type.  The inverse
+//   conversion serves mamba_save_weights.
 #include "common.cuh"
 
 namespace mb {
@@ -73,6 +74,23 @@ __global__ void transpose_cast_kernel(const float *__restrict__ src, T *__restri
     }
 }
 
+// dst[k, n] = src[n, k] widened to FP32 (src [N, K] in the activation type):
+// the inverse of transpose_cast, for writing weights back out as a blob.
+template <typename T>
+__global__ void untranspose_widen_kernel(const T *__restrict__ src, float *__restrict__ dst, int K, int N) {
+    __shared__ float tile[32][33];
+    const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < K) tile[r][threadIdx.x] = cvt_f32(src[(int64_t)n * K + k]);
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int k = k0 + r, n = n0 + threadIdx.x;
+        if (k < K && n < N) dst[(int64_t)k * N + n] = tile[threadIdx.x][r];
+    }
+}
+
 }  // namespace
 
 uint64_t fill_key(uint64_t seed, int layer, int tag) {
@@ -117,6 +135,16 @@ int transpose_cast(const float *src, void *dst, int dtype, int K, int N, cudaStr
     else
         transpose_cast_kernel<float><<<grid, block, 0, st>>>(src, static_cast<float *>(dst), K, N);
     return launch_status("transpose_cast kernel");
+}
+
+int untranspose_widen(const void *src, float *dst, int dtype, int K, int N, cudaStream_t st) {
+    if (K <= 0 || N <= 0) return 0;
+    dim3 grid(ceil_div(K, 32), ceil_div(N, 32)), block(32, 8);
+    if (dtype == MAMBA_F16)
+        untranspose_widen_kernel<__half><<<grid, block, 0, st>>>(static_cast<const __half *>(src), dst, K, N);
+    else
+        untranspose_widen_kernel<float><<<grid, block, 0, st>>>(static_cast<const float *>(src), dst, K, N);
+    return launch_status("untranspose_widen kernel");
 }
 
 }  // namespace mb

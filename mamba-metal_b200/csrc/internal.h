@@ -61,5 +61,6 @@ int fill_random(void *out, int dtype, int64_t n, uint64_t key, int dist, float p
 int fill_A(float *A, int D, int N, cudaStream_t st);
 int fill_const(float *p, int64_t n, float v, cudaStream_t st);
 int transpose_cast(const float *src, void *dst, int dtype, int K, int N, cudaStream_t st);
+int untranspose_widen(const void *src, float *dst, int dtype, int K, int N, cudaStream_t st);
 
 }  // namespace mb

@@ -521,29 +521,43 @@ struct Model {
             io_events.push_back(e);
         }
         const size_t row_elems = (size_t)L * M;
+        // Errors inside the loops stop further enqueues but never return
+        // early: the copies already queued read `in` and write `out`, so all
+        // three streams are drained before returning, error or not.
         int err = 0;
-        for (int k = 0; k < chunks; ++k) {
-            const int r0 = starts[k], nr = starts[k + 1] - r0;
-            if (nr <= 0) break;
-            MB_CUDA_TRY(cudaMemcpyAsync(d + r0 * row_elems, in + r0 * row_elems, sizeof(float) * nr * row_elems,
-                                        cudaMemcpyHostToDevice, h2d));
-            MB_CUDA_TRY(cudaEventRecord(io_events[2 * k], h2d));
-        }
+        auto note = [&](cudaError_t e, const char *what) {
+            if (e != cudaSuccess && !err) {
+                set_error(std::string("forward: ") + what + ": " + cudaGetErrorString(e));
+                err = -1;
+            }
+        };
+        int uploaded = 0;
         for (int k = 0; k < chunks && !err; ++k) {
             const int r0 = starts[k], nr = starts[k + 1] - r0;
             if (nr <= 0) break;
+            note(cudaMemcpyAsync(d + r0 * row_elems, in + r0 * row_elems, sizeof(float) * nr * row_elems,
+                                 cudaMemcpyHostToDevice, h2d),
+                 "host-to-device copy");
+            if (!err) note(cudaEventRecord(io_events[2 * k], h2d), "event record");
+            if (!err) uploaded = k + 1;
+        }
+        for (int k = 0; k < uploaded && !err; ++k) {
+            const int r0 = starts[k], nr = starts[k + 1] - r0;
+            if (nr <= 0) break;
             float *dk = d + r0 * row_elems;
-            MB_CUDA_TRY(cudaStreamWaitEvent(st, io_events[2 * k], 0));
+            note(cudaStreamWaitEvent(st, io_events[2 * k], 0), "stream wait");
+            if (err) break;
             if (forward_device(dk, dk, nr, L, st)) {
                 err = -1;
                 break;
             }
-            MB_CUDA_TRY(cudaEventRecord(io_events[2 * k + 1], st));
-            MB_CUDA_TRY(cudaStreamWaitEvent(d2h, io_events[2 * k + 1], 0));
-            MB_CUDA_TRY(cudaMemcpyAsync(out + r0 * row_elems, dk, sizeof(float) * nr * row_elems,
-                                        cudaMemcpyDeviceToHost, d2h));
+            note(cudaEventRecord(io_events[2 * k + 1], st), "event record");
+            if (!err) note(cudaStreamWaitEvent(d2h, io_events[2 * k + 1], 0), "stream wait");
+            if (!err)
+                note(cudaMemcpyAsync(out + r0 * row_elems, dk, sizeof(float) * nr * row_elems,
+                                     cudaMemcpyDeviceToHost, d2h),
+                     "device-to-host copy");
         }
-        // every queued copy and kernel finishes before returning, error or not
         const cudaError_t e1 = cudaStreamSynchronize(h2d);
         const cudaError_t e2 = cudaStreamSynchronize(st);
         const cudaError_t e3 = cudaStreamSynchronize(d2h);
@@ -808,6 +822,56 @@ static int load_weights(Model &m, const void *data, size_t size) {
     return 0;
 }
 
+// Writes the model's weights as a blob that load_weights accepts: projections
+// widened back to FP32 [K, N] (exactly the values the GEMMs use, i.e. already
+// rounded to the activation type), per-channel vectors copied as stored.
+static int save_weights(Model &m, void *data, size_t size) {
+    MB_CHECK_ARG(data != nullptr, "save_weights: null blob");
+    const size_t per = layer_floats(m.cfg);
+    MB_CHECK_ARG(size == kBlobHeader + per * 4 * (size_t)m.cfg.n_layer,
+                 "save_weights: blob size differs from mamba_weights_blob_size");
+    char *p = static_cast<char *>(data);
+    std::memset(p, 0, kBlobHeader);
+    std::memcpy(p, kBlobMagic, 8);
+    std::memcpy(p + 8, &kBlobVersion, 4);
+    std::memcpy(p + 12, &kBlobHeader, 4);
+    std::memcpy(p + 16, &m.cfg, sizeof(MambaConfig));
+    const int32_t r = m.R;
+    std::memcpy(p + 40, &r, 4);
+    DeviceBuffer stage;
+    if (stage.reserve(per * 4)) return -1;
+    const int M = m.M, D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
+    cudaStream_t st = m.stream;
+    for (int l = 0; l < m.cfg.n_layer; ++l) {
+        float *s = static_cast<float *>(stage.ptr);
+        const LayerWeights &w = m.layers[l];
+        if (untranspose_widen(w.w_in_t, s, m.act, M, 2 * D, st)) return -1;
+        s += (size_t)M * 2 * D;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.conv_w, (size_t)D * K * 4, cudaMemcpyDeviceToDevice, st));
+        s += (size_t)D * K;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.conv_b, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        s += D;
+        if (untranspose_widen(w.w_x_t, s, m.act, D, XD, st)) return -1;
+        s += (size_t)D * XD;
+        if (untranspose_widen(w.w_dt_t, s, m.act, R, D, st)) return -1;
+        s += (size_t)R * D;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.A, (size_t)D * N * 4, cudaMemcpyDeviceToDevice, st));
+        s += (size_t)D * N;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.Dskip, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        s += D;
+        if (untranspose_widen(w.w_out_t, s, m.act, D, M, st)) return -1;
+        s += (size_t)D * M;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.norm_w, (size_t)M * 4, cudaMemcpyDeviceToDevice, st));
+        s += M;
+        MB_CUDA_TRY(cudaMemcpyAsync(s, w.dt_bias, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
+        char *dst = p + kBlobHeader + per * 4 * (size_t)l;
+        MB_CUDA_TRY(cudaMemcpyAsync(dst, stage.ptr, per * 4, cudaMemcpyDeviceToHost, st));
+        // The staging buffer is reused by the next layer.
+        MB_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return 0;
+}
+
 enum Tag { kTagIn = 1, kTagConvW, kTagConvB, kTagX, kTagDt, kTagOut, kTagDtBias };
 
 static int init_random(Model &m, uint64_t seed) {
@@ -990,6 +1054,21 @@ int mamba_init_weights_random(MambaModel *m, uint64_t seed) {
     }
     mb::DeviceGuard g(m->rt->dev);
     return mb::init_random(*m->rt, seed) ? -1 : 0;
+}
+
+int mamba_save_weights(MambaModel *m, void *blob, size_t size) {
+    mb::clear_error();
+    if (!m || !m->rt) {
+        set_error("mamba_save_weights: null model");
+        return -1;
+    }
+    mb::DeviceGuard g(m->rt->dev);
+    // Weights may still be written by work queued on the caller's stream.
+    if (cudaStreamSynchronize(m->rt->cur_stream()) != cudaSuccess) {
+        set_error("mamba_save_weights: stream error");
+        return -1;
+    }
+    return mb::save_weights(*m->rt, blob, size) ? -1 : 0;
 }
 
 int mamba_forward_device(MambaModel *m, const float *input, float *output, int batch, int seq_len,

@@ -1095,21 +1095,50 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 namespace {
 
-// Device address of g_noalloc_scratch on the current device (resolved on the
-// first call on each device, with that device current).
+// The calling thread's current driver context, through the runtime's
+// driver entry point (the library links only the runtime).
+CUcontext current_context() {
+    using GetCtx = CUresult (*)(CUcontext *);
+    static GetCtx fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetCtx>(f);
+    });
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+// Device address of g_noalloc_scratch on the current device, resolved with
+// that device current on the first call there.  The address is cached with
+// the context it was resolved in: after a device reset the module is loaded
+// again in a new context, possibly elsewhere, and the address is looked up
+// again.  (A thread that has not yet touched the device reports no context;
+// the lookup itself then makes the primary context current.)
 int noalloc_scratch(void **out) {
     static std::mutex mu;
-    static std::vector<void *> cache;
+    struct Slot {
+        CUcontext ctx = nullptr;
+        void *ptr = nullptr;
+    };
+    static std::vector<Slot> cache;
     int dev = 0;
     MB_CUDA_TRY(cudaGetDevice(&dev));
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lk(mu);
-    if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
-    if (!cache[dev]) {
+    if ((int)cache.size() <= dev) cache.resize(dev + 1);
+    Slot &sl = cache[dev];
+    if (!sl.ptr || !ctx || sl.ctx != ctx) {
         void *p = nullptr;
         MB_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        cache[dev] = p;
+        sl.ptr = p;
+        sl.ctx = ctx;
     }
-    *out = cache[dev];
+    *out = sl.ptr;
     return 0;
 }
 

@@ -84,6 +84,7 @@ _PROTOTYPES = {
     "mamba_dt_rank": (c_int, [ctypes.POINTER(MambaConfig)]),
     "mamba_weights_blob_size": (c_size, [ctypes.POINTER(MambaConfig)]),
     "mamba_init_weights_random": (c_int, [c_void_p, ctypes.c_uint64]),
+    "mamba_save_weights": (c_int, [c_void_p, c_void_p, c_size]),
     "mamba_forward_device": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "mamba_step_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mamba_state_batch": (c_int, [c_void_p]),
@@ -186,6 +187,29 @@ def make_weight_blob(cfg, layers):
     return b"".join(parts)
 
 
+def weights_from_blob(cfg, blob):
+    """Per-layer dicts of FP32 numpy views into a weight blob (the inverse of
+    make_weight_blob; no copies).  blob: bytes, bytearray or a uint8 array."""
+    shapes = layer_shapes(cfg)
+    buf = np.frombuffer(blob, dtype=np.uint8)
+    if bytes(buf[:8]) != b"MAMBAB2\0":
+        raise ValueError("not a weight blob (bad magic)")
+    per = sum(int(np.prod(shapes[n])) for n in LAYER_TENSORS)
+    floats = buf[64:].view(np.float32)
+    if floats.size != per * cfg.n_layer:
+        raise ValueError("blob holds %d floats, config needs %d" % (floats.size, per * cfg.n_layer))
+    layers = []
+    off = 0
+    for _ in range(cfg.n_layer):
+        lw = {}
+        for name in LAYER_TENSORS:
+            n = int(np.prod(shapes[name]))
+            lw[name] = floats[off:off + n].reshape(shapes[name])
+            off += n
+        layers.append(lw)
+    return layers
+
+
 def random_layer_weights(cfg, rng):
     """Synthetic FP32 weights with the documented distributions (numpy RNG):
     linear ~ N(0, 0.02); conv1d, conv_bias ~ U(-0.5, 0.5);
@@ -234,11 +258,25 @@ class Model:
         return self._h
 
     def load_weights(self, blob):
+        if isinstance(blob, np.ndarray):
+            blob = np.ascontiguousarray(blob, dtype=np.uint8)
+            _check(lib().mamba_load_weights(self._h, blob.ctypes.data, blob.nbytes), "mamba_load_weights")
+            return
         buf = ctypes.create_string_buffer(blob, len(blob)) if isinstance(blob, bytes) else blob
         _check(lib().mamba_load_weights(self._h, buf, len(blob)), "mamba_load_weights")
 
     def init_random(self, seed):
         _check(lib().mamba_init_weights_random(self._h, seed), "mamba_init_weights_random")
+
+    def save_weights(self):
+        """The model's weights as a blob (mamba_save_weights): a numpy uint8
+        array that load_weights and weights_from_blob accept."""
+        size = lib().mamba_weights_blob_size(ctypes.byref(self.cfg))
+        if size == 0:
+            raise MambaError("mamba_weights_blob_size: bad config")
+        blob = np.empty(size, dtype=np.uint8)
+        _check(lib().mamba_save_weights(self._h, blob.ctypes.data, size), "mamba_save_weights")
+        return blob
 
     def forward(self, x, out=None):
         """Host FP32 [batch, L, d_model] numpy in, numpy out (mamba_forward)."""
@@ -322,6 +360,15 @@ class State:
                "mamba_state_buffers")
         return c.value, s.value
 
+    def tensors(self, layer):
+        """Zero-copy torch views of one layer's FP32 state on the device:
+        (conv_state [batch, d_inner, d_conv-1], ssm_state [batch, d_inner,
+        d_state]).  Valid while this state handle lives."""
+        cfg = self.model.cfg
+        c, s = self.buffers(layer)
+        return (_device_view(c, (self.batch, cfg.d_inner, cfg.d_conv - 1)),
+                _device_view(s, (self.batch, cfg.d_inner, cfg.d_state)))
+
 
 # ---------------------------------------------------------------------------
 # Kernel-level helpers on torch CUDA tensors
@@ -342,6 +389,20 @@ def _dt(t):
 
 def _ptr(t):
     return None if t is None else t.data_ptr()
+
+
+class _CudaArray:
+    """Describes library-owned device memory through __cuda_array_interface__
+    so torch can view it without a copy."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 2, "strides": None}
+
+
+def _device_view(ptr, shape, typestr="<f4"):
+    torch = _torch()
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device="cuda")
 
 
 def _stream(stream):

@@ -95,6 +95,35 @@ def block_step(h_t, w, conv_state, ssm_state, cfg, act):
     return h_t + _mm(y, rnd(w["out_proj"], act))
 
 
+def model_decode(h_seq, layers, cfg, act, state=None):
+    """T decode steps from `state` (zeros when None): h_seq FP32 [batch, T,
+    d_model] -> outputs [batch, T, d_model].  The same arithmetic as calling
+    model_step T times (conv and SSM updates via the step restatements, token
+    by token), ordered layer by layer: a layer's projections act row-wise,
+    so they run on all T tokens at once and each layer's weights are read
+    once instead of T times."""
+    h = np.array(h_seq, dtype=np.float32, copy=True)
+    bsz, T, M = h.shape
+    D, N, R = cfg.d_inner, cfg.d_state, cfg.dt_rank
+    conv, ssm = state if state is not None else new_state(cfg, bsz)
+    for l, w in enumerate(layers):
+        hn = rnd(oracle.rmsnorm(h.reshape(bsz * T, M), w["norm_weight"], EPS), act)
+        xz = rnd(_mm(hn, rnd(w["in_proj"], act)), act).reshape(bsz, T, 2 * D)
+        u = np.empty((bsz, T, D), np.float32)
+        for t in range(T):
+            u[:, t] = rnd(oracle.causal_conv1d_step(xz[:, t, :D], w["conv1d"], w["conv_bias"], conv[l],
+                                                    silu=True), act)
+        xdbc = rnd(_mm(u.reshape(bsz * T, D), rnd(w["x_proj"], act)), act).reshape(bsz, T, R + 2 * N)
+        draw = rnd(_mm(xdbc[..., :R].reshape(bsz * T, R), rnd(w["dt_proj"], act)), act).reshape(bsz, T, D)
+        y = np.empty((bsz, T, D), np.float32)
+        for t in range(T):
+            y[:, t] = oracle.ssm_step(u[:, t], draw[:, t], xdbc[:, t, R:R + N], xdbc[:, t, R + N:], w["A"],
+                                      w["D"], ssm[l], z=xz[:, t, D:], dt_bias=w["dt_bias"])
+        y = rnd(y, act)
+        h = h + _mm(y.reshape(bsz * T, D), rnd(w["out_proj"], act)).reshape(bsz, T, M)
+    return h
+
+
 def model_step(h_t, layers, state, cfg, act):
     conv, ssm = state
     h_t = np.asarray(h_t, np.float32)

@@ -8,6 +8,9 @@ Outputs:
                                (only when that tree is present; the prebuilt
                                library is what travels to GPU machines).
 
+The reference tree is $MAMBA_REF, or by default a checkout named `reference`
+next to this repository's root directory.
+
 Both builds use -ffp-contract=off so the compiler never fuses a multiply and
 an add, which keeps the restatement bit-identical to the reference build.
 """
@@ -18,12 +21,13 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 REF_OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+REPO = os.path.dirname(HERE)
 
 
 def reference_root():
-    """Location of the reference checkout (env MAMBA_REF overrides)."""
-    return os.environ.get("MAMBA_REF", DEFAULT_REF)
+    """Location of the reference checkout: $MAMBA_REF when set, else a
+    directory named `reference` beside this repository's root."""
+    return os.environ.get("MAMBA_REF") or os.path.join(os.path.dirname(REPO), "reference")
 
 
 def _run(cmd):
@@ -54,6 +58,10 @@ def build_reference(force=False):
     ref_src = os.path.join(cpu_dir, "selective_scan_cpu.cpp")
     out = os.path.join(REF_OUT, "libref_scan.so")
     if not os.path.exists(ref_src):
+        if os.environ.get("MAMBA_REF"):
+            raise FileNotFoundError("MAMBA_REF=%s has no Sources/CPURef/selective_scan_cpu.cpp" % ref)
+        # No checkout here (e.g. a GPU machine): use the prebuilt library if
+        # it travelled with the tree.
         return out if os.path.exists(out) else None
     os.makedirs(REF_OUT, exist_ok=True)
     shim = os.path.join(HERE, "ref_shim.cpp")

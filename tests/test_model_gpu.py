@@ -233,3 +233,24 @@ def test_chunked_host_forward_matches_device_forward(cuda, monkeypatch):
     assert oracle.normwise_rel_err(out - h, ref - h) < 2e-3
     ref_cpu = block_ref.model_forward(h, layers, cfg, block_ref.F16)
     assert oracle.normwise_rel_err(out - h, ref_cpu - h) < 2e-3
+
+
+def test_save_weights_round_trip(cuda):
+    """mamba_save_weights writes a blob that reproduces the model bit for bit
+    when loaded into a second model; its projections are the FP16 values the
+    GEMMs use, so saving a loaded blob of FP16-exact weights gives it back."""
+    a = mb.Model(96, 16, 4, 2, 2, mb.F16)
+    a.init_random(11)
+    blob = a.save_weights()
+    assert blob.nbytes == mb.lib().mamba_weights_blob_size(ctypes.byref(a.cfg))
+    b = mb.Model(96, 16, 4, 2, 2, mb.F16)
+    b.load_weights(blob)
+    h = np.random.default_rng(1).standard_normal((2, 33, 96)).astype(np.float32)
+    assert np.array_equal(a.forward(h), b.forward(h))
+    assert np.array_equal(b.save_weights(), blob)
+    layers = mb.weights_from_blob(a.cfg, blob)
+    assert np.array_equal(layers[1]["A"], np.tile(-np.arange(1, 17, dtype=np.float32), (192, 1)))
+    w = layers[0]["in_proj"]
+    assert np.array_equal(w, w.astype(np.float16).astype(np.float32))
+    assert mb.lib().mamba_save_weights(a.handle, blob.ctypes.data, blob.nbytes - 4) == -1
+    assert "size" in mb.last_error()

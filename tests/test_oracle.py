@@ -208,6 +208,42 @@ def test_block_step_matches_block_forward():
         assert oracle.normwise_rel_err(y_step, y_fwd) < tol
 
 
+def test_layer_major_decode_equals_token_steps():
+    """block_ref.model_decode (projections batched over the tokens of a layer)
+    gives the outputs and the final states of model_step called token by
+    token; only the BLAS summation order of the batched products differs."""
+    from mamba_b200 import MambaConfig, random_layer_weights
+    cfg = MambaConfig(48, 16, 4, 2, 3, block_ref.F16)
+    rng = np.random.default_rng(9)
+    layers = [random_layer_weights(cfg, rng) for _ in range(cfg.n_layer)]
+    bsz, T = 3, 7
+    h = rng.standard_normal((bsz, T, cfg.d_model)).astype(np.float32)
+    s_tok = block_ref.new_state(cfg, bsz)
+    y_tok = np.stack([block_ref.model_step(h[:, t], layers, s_tok, cfg, block_ref.F16) for t in range(T)], 1)
+    s_lay = block_ref.new_state(cfg, bsz)
+    y_lay = block_ref.model_decode(h, layers, cfg, block_ref.F16, state=s_lay)
+    assert oracle.normwise_rel_err(y_lay - h, y_tok - h) < 1e-4
+    for a, b in zip(s_lay[1], s_tok[1]):
+        assert oracle.normwise_rel_err(a, b) < 1e-4
+
+
+def test_weight_blob_round_trip():
+    """weights_from_blob reads back exactly what make_weight_blob wrote (views
+    into the blob, layer by layer, in the documented tensor order)."""
+    import mamba_b200 as mb
+    cfg = mb.MambaConfig(40, 5, 3, 3, 2, mb.F16)
+    rng = np.random.default_rng(10)
+    layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
+    blob = mb.make_weight_blob(cfg, layers)
+    back = mb.weights_from_blob(cfg, blob)
+    for a, b in zip(layers, back):
+        assert set(a) == set(b)
+        for k in a:
+            assert np.array_equal(a[k], b[k]), k
+    with pytest.raises(ValueError):
+        mb.weights_from_blob(mb.MambaConfig(40, 5, 3, 3, 3, mb.F16), blob)
+
+
 def _propagate_loop(carries):
     """Pure-Python restatement of propagate_tile_carries_f32
     (prefix_scan.metal:19-40) with the documented [tiles, width, 2] layout:

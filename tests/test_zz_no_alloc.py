@@ -58,20 +58,18 @@ def _run_pair(inputs):
     return (y_ws, h_ws), (y_na, h_na)
 
 
-def _rel(a, b):
-    a, b = a.double(), b.double()
-    return float((a - b).abs().max() / b.abs().max())
-
-
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.float16, 2e-3)])
-def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(dtype, tol):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(dtype):
     # batch 1 x 256 channels is too few CTAs to fill the GPU, so time is split
-    # into chunks and the carries go through scratch memory.
+    # into chunks and the carries go through scratch memory.  Both entry
+    # points run the same kernels with the same chunk length, so the results
+    # must agree bit for bit (a wrong offset into the scratch array or a carry
+    # left over from the previous call would show up here).
     for seed in (11, 12):  # two calls in a row, different data
         (y_ws, h_ws), (y_na, h_na) = _run_pair(_inputs(seed, 1, 4096, 256, 16, dtype))
         assert torch.isfinite(y_na.float()).all()
-        assert _rel(y_na, y_ws) <= tol
-        assert _rel(h_na, h_ws) <= 1e-5
+        assert torch.equal(y_na, y_ws)
+        assert torch.equal(h_na, h_ws)
 
 
 def test_noalloc_rejects_sizes_beyond_its_static_scratch():
