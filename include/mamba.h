@@ -103,6 +103,8 @@ const char *mamba_last_error(void);
  * its outputs are invalid.  Bit 1: the same for a wait inside
  * mamba_gated_mlp_up.  Bit 2: the same for mamba_linear (and the decode
  * projections that use it).  Bit 3: set by mamba_selftest_bounded_wait.
+ * Bit 4: the same as bit 0 for the CTA-pair projection GEMM (the model's
+ * forward projections, mamba_linear above 512 rows).
  * Waits for the device; clear != 0 resets them. */
 unsigned mamba_device_status(int clear);
 
@@ -341,13 +343,16 @@ int mamba_gated_silu_mul(const void *gate, const void *up, void *out, int64_t n,
  * x FP16 [rows, k] with row stride ldx elements; w FP16 [n, k] (the
  * reference's [k, n] weight transposed, i.e. K-major); bias FP32 [n] or
  * NULL; y row stride ldy elements.  FP32 accumulation.  k and n multiples
- * of 8, ldx and ldy multiples of 8, pointers 16-byte aligned.  Built for few rows (decode):
- * K is split across CTAs when the output blocks cannot fill the GPU, which
- * needs a workspace of mamba_linear_workspace(rows, n, k) bytes (0 when no
- * split is made; 16-byte aligned) for the FP32 partials, summed in split
- * order by a second kernel (results do not depend on CTA timing).  Calls
- * sharing a workspace must not overlap on the GPU.  Needs a compute
- * capability 10.x GPU. */
+ * of 8, ldx and ldy multiples of 8, pointers 16-byte aligned.  Up to 512
+ * rows (decode sizes): one CTA per 256-row block, K split across CTAs when
+ * the output blocks cannot fill the GPU, which needs a workspace of
+ * mamba_linear_workspace(rows, n, k) bytes (0 when no split is made;
+ * 16-byte aligned) for the FP32 partials, summed in split order by a second
+ * kernel (results do not depend on CTA timing).  Calls sharing a workspace
+ * must not overlap on the GPU.  Above 512 rows: the persistent CTA-pair
+ * kernel the model's forward projections use (256 x 256 tiles, M = 256
+ * pair MMAs, bulk tensor stores; mode 1 adds with bulk tensor adds), no
+ * workspace.  Needs a compute capability 10.x GPU. */
 size_t mamba_linear_workspace(int64_t rows, int n, int k);
 int mamba_linear(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t rows,
                  int n, int k, int mode, void *workspace, size_t workspace_bytes, void *stream);

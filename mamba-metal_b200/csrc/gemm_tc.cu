@@ -1,0 +1,420 @@
+// gemm_tc.cu -- the Mamba block's projections on the fifth-generation
+// tensor cores: C = A @ W^T with FP16 operands and FP32 accumulation, the
+// job of linear_f16 (Sources/Kernels/projection.metal:32-49) for the
+// in_proj, x_proj, dt_proj and out_proj GEMMs of the layer graph
+// (Sources/Mamba/MambaRuntime.cpp:93-101).
+//
+//   A  FP16 [M, K] rows of lda elements (activations, K-major)
+//   W  FP16 [N, K] (the reference's [K, N] weight transposed once at load)
+//   C  [M, N] rows of ldc elements; epilogues (bias: optional FP32 [N]):
+//        kProjF16     C (FP16)  = acc + bias      (in_proj, x_proj, dt_proj)
+//        kProjF32Add  C (FP32) += acc + bias      (out_proj into the residual)
+//        kProjF32     C (FP32)  = acc + bias
+//
+// Structure: a persistent kernel run by CTA pairs (thread-block clusters of
+// two, cta_group::2).  A pair owns a 256 x BN output tile (BN <= 256): each
+// CTA loads 128 rows of A and BN/2 rows of W per 64-wide K block by TMA
+// (128-byte swizzle) into its own 5-stage ring, and one thread of the even
+// CTA issues tcgen05.mma with M = 256 that reads both CTAs' shared memory
+// and accumulates in both CTAs' TMEM (each CTA gets its 128 rows).  Per SM
+// and K block that is 32 KB of operands for a 128 x 256 x 64 slab, two
+// thirds of what one CTA alone would load for the same slab.  TMEM holds two
+// accumulators, so the epilogue of one tile overlaps the MMAs of the next.
+//
+// Roles (192 threads per CTA):
+//   warp 0 lane 0  TMA producer.  Its copies complete on the even CTA's
+//                  stage barrier, which expects the bytes of both CTAs.
+//   warp 1         TMEM owner (both CTAs); in the even CTA one lane issues
+//                  the MMAs and commits them to both CTAs' barriers.
+//   warps 2-5      epilogue: TMEM -> registers -> a 128-byte-swizzled
+//                  shared-memory box of 32 rows per warp -> bulk tensor store
+//                  (or bulk tensor add for the residual), double-buffered
+//                  per warp; then the warp releases the accumulator to the
+//                  even CTA's MMA thread.
+// Every mbarrier wait is bounded (2 s); on timeout the role stops, bit 4 of
+// the device status is set, and both CTAs still reach the final cluster
+// barrier, so TMEM is freed and neither CTA exits while its peer may touch
+// its shared memory.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace mb {
+
+__device__ unsigned int g_proj_error = 0;
+
+namespace {
+
+constexpr int kPBK = 64;                          // K per stage: one 128-byte swizzle row
+constexpr int kPUK = 16;                          // K per MMA
+constexpr int kPStages = 5;
+constexpr int kPThreads = 192;
+constexpr int kPAccCols = 256;                    // TMEM columns per accumulator
+constexpr int kPTmemCols = 2 * kPAccCols;
+constexpr int kPStageA = 128 * kPBK * 2;          // 16 KB: this CTA's 128 rows of A
+constexpr int kPStageB = 128 * kPBK * 2;          // 16 KB: up to 128 rows of W
+constexpr int kPStage = kPStageA + kPStageB;
+constexpr int kPEpiBox = 32 * 128;                // 4 KB: 32 rows x 128 bytes
+constexpr int kPEpiBytes = 4 * 2 * kPEpiBox;      // 4 warps x 2 buffers
+constexpr int kPSmem = kPStages * kPStage + kPEpiBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr unsigned kErrProjTimeout = 16u;
+
+struct ProjParams {
+    const float *bias;  // [N] FP32 added to every row, or NULL
+    int M, N, K;
+    int BN;          // output columns per tile (multiple of 16, <= 256)
+    int m_tiles, n_tiles, kblocks;
+    int mode;
+    uint32_t idesc;
+    uint32_t tx_bytes;  // operand bytes of one stage, both CTAs
+};
+
+__device__ __forceinline__ bool warp_wait_p(uint64_t *bar, uint32_t parity) {
+    int ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(uint32_t a, uint32_t b) {
+    const __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Row `r` of a 32-row box of 128-byte rows with the TMA 128-byte swizzle:
+// 16-byte chunk j lands at chunk j ^ (r % 8).
+__device__ __forceinline__ void st_swizzled(uint8_t *box, int r, int j, uint4 v) {
+    *reinterpret_cast<uint4 *>(box + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+}
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_c, const ProjParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *epi = smem + kPStages * kPStage;
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi + kPEpiBytes);
+    uint64_t *empty = full + kPStages;
+    uint64_t *tfull = empty + kPStages;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+    const uint32_t rank = cluster_ctarank();  // 0: the pair's MMA issuer
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles = p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+        prefetch_tensormap(&map_a);
+        prefetch_tensormap(&map_b);
+        prefetch_tensormap(&map_c);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, kPTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // stage barriers of the even CTA
+            const int half = p.BN >> 1;
+            uint32_t it = 0;
+            for (int tile = pair; tile < tiles && ok; tile += npairs) {
+                const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+                const int arow = mt * 256 + (int)rank * 128, brow = nt * p.BN + (int)rank * half;
+                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                    const uint32_t s = it % kPStages, ph = (it / kPStages) & 1;
+                    if (!mbar_wait_bounded(&empty[s], ph ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], p.tx_bytes);
+                    uint8_t *a = smem + s * kPStage;
+                    tma_load_2d_pair(a, &map_a, full0 + s * 8, kb * kPBK, arow);
+                    tma_load_2d_pair(a + kPStageA, &map_b, full0 + s * 8, kb * kPBK, brow);
+                }
+            }
+            // The even CTA sees every copy of both CTAs land before it exits.
+            if (rank == 0) {
+                const uint32_t first = it > (uint32_t)kPStages ? it - kPStages : 0;
+                for (uint32_t j = first; j < it; ++j)
+                    if (!mbar_wait_bounded_cluster(&full[j % kPStages], (j / kPStages) & 1)) ok = false;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            uint32_t it = 0, tcount = 0;
+            for (int tile = pair; tile < tiles && ok; tile += npairs, ++tcount) {
+                const uint32_t b = tcount & 1, tph = (tcount >> 1) & 1;
+                if (!mbar_wait_bounded_cluster(&tempty[b], tph ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + b * kPAccCols;
+                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                    const uint32_t s = it % kPStages, ph = (it / kPStages) & 1;
+                    if (!mbar_wait_bounded_cluster(&full[s], ph)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * kPStage);
+                    const uint32_t b_addr = a_addr + kPStageA;
+#pragma unroll
+                    for (int k = 0; k < kPBK / kPUK; ++k)
+                        umma_f16_pair(d_tmem, smem_desc_sw128(a_addr + k * kPUK * 2),
+                                      smem_desc_sw128(b_addr + k * kPUK * 2), p.idesc, (kb | k) != 0);
+                    umma_commit_pair(&empty[s], 0x3);  // the stage is free in both CTAs once read
+                }
+                if (!ok) break;
+                umma_commit_pair(&tfull[b], 0x3);  // accumulator b holds the finished tile
+            }
+            // Every issued MMA completes before TMEM may be freed.
+            umma_commit_pair(drain, 0x1);
+            if (!mbar_wait_bounded(drain, 0)) ok = false;
+        }
+    } else {
+        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows
+        // 32*(w%4) .. +31 of this CTA's 128.
+        const int quarter = warp & 3;
+        uint8_t *boxes = epi + (warp - 2) * 2 * kPEpiBox;
+        const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+        const bool f16 = p.mode == kProjF16;
+        const int cstep = f16 ? 64 : 32;
+        uint32_t tcount = 0, nbox = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++tcount) {
+            const uint32_t b = tcount & 1, tph = (tcount >> 1) & 1;
+            if (!warp_wait_p(&tfull[b], tph)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+            const int row0 = mt * 256 + (int)rank * 128 + quarter * 32;
+            const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + b * kPAccCols;
+            for (int c = 0; c < p.BN; c += cstep) {
+                const int col = nt * p.BN + c;
+                uint32_t v0[32], v1[32];
+                tmem_ld_32x32b_x32(tl + c, v0);
+                if (f16) tmem_ld_32x32b_x32(tl + c + 32, v1);
+                tmem_wait_ld();
+                if (col >= p.N || row0 >= p.M) continue;  // nothing of this box is inside C
+                if (p.bias) {
+                    // every lane reads the same bias entries (broadcast loads)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col + j < p.N) v0[j] = __float_as_uint(__uint_as_float(v0[j]) + p.bias[col + j]);
+                    if (f16) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col + 32 + j < p.N)
+                                v1[j] = __float_as_uint(__uint_as_float(v1[j]) + p.bias[col + 32 + j]);
+                    }
+                }
+                uint8_t *box = boxes + (nbox & 1) * kPEpiBox;
+                // the bulk store that last read this box has finished reading it
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                if (f16) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        st_swizzled(box, lane, j,
+                                    make_uint4(pack_half2(v0[8 * j], v0[8 * j + 1]),
+                                               pack_half2(v0[8 * j + 2], v0[8 * j + 3]),
+                                               pack_half2(v0[8 * j + 4], v0[8 * j + 5]),
+                                               pack_half2(v0[8 * j + 6], v0[8 * j + 7])));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        st_swizzled(box, lane, 4 + j,
+                                    make_uint4(pack_half2(v1[8 * j], v1[8 * j + 1]),
+                                               pack_half2(v1[8 * j + 2], v1[8 * j + 3]),
+                                               pack_half2(v1[8 * j + 4], v1[8 * j + 5]),
+                                               pack_half2(v1[8 * j + 6], v1[8 * j + 7])));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        st_swizzled(box, lane, j, make_uint4(v0[4 * j], v0[4 * j + 1], v0[4 * j + 2], v0[4 * j + 3]));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (p.mode == kProjF32Add)
+                        tma_reduce_add_2d(&map_c, box, col, row0);
+                    else
+                        tma_store_2d(&map_c, box, col, row0);
+                    bulk_commit_group();
+                }
+                ++nbox;
+            }
+            // accumulator b is read: hand it back to the even CTA's MMA thread
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0)
+                    mbar_arrive(&tempty[b]);
+                else
+                    mbar_arrive_cluster(tempty0 + b * 8);
+            }
+        }
+        if (lane == 0) bulk_wait_group_all();
+        __syncwarp();
+    }
+    if (!ok) atomicOr(&g_proj_error, kErrProjTimeout);
+    tc_fence_before();
+    cluster_sync();  // nothing of either CTA touches TMEM or the peer's shared memory after this
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, kPTmemCols);
+    }
+}
+
+// 2-D map over a row-major [rows, cols] matrix (row stride ld elements) with
+// box [box_rows, box_cols] and the 128-byte swizzle; loads outside the
+// matrix read zeros, stores outside it are dropped.
+bool encode_2d(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *ptr, int64_t rows, int64_t cols,
+               int64_t ld, int box_cols, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, t, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Per-device launch facts: the shared-memory opt-in and how many CTA pairs
+// of this kernel fit on the GPU at once (clusters must sit inside one GPC).
+struct DevInfo {
+    bool ready = false;
+    int pairs = 0;
+};
+
+int device_info(DevInfo &out) {
+    static std::mutex mu;
+    static std::vector<DevInfo> cache;
+    int dev = 0;
+    MB_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1);
+    DevInfo &d = cache[dev];
+    if (!d.ready) {
+        MB_CUDA_TRY(cudaFuncSetAttribute(proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr{};
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * 148, 1, 1);
+        cfg.blockDim = dim3(kPThreads, 1, 1);
+        cfg.dynamicSmemBytes = kPSmem;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        MB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, proj_gemm_kernel, &cfg));
+        MB_CHECK_ARG(n > 0, "proj_gemm: no CTA pair fits on this GPU");
+        d.pairs = n;
+        d.ready = true;
+    }
+    out = d;
+    return 0;
+}
+
+}  // namespace
+
+int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void *C, int64_t ldc, int64_t M, int N,
+              int K, int mode, cudaStream_t st) {
+    MB_CHECK_ARG(M >= 0 && N > 0 && K > 0, "proj_gemm: bad sizes");
+    if (M == 0) return 0;
+    MB_CHECK_ARG(A && W && C, "proj_gemm: null pointer");
+    MB_CHECK_ARG(mode == kProjF16 || mode == kProjF32Add || mode == kProjF32, "proj_gemm: bad epilogue mode");
+    MB_CHECK_ARG(K % 8 == 0 && lda % 8 == 0 && lda >= K, "proj_gemm: K and lda must be multiples of 8, lda >= K");
+    const int cs = mode == kProjF16 ? 2 : 4;
+    MB_CHECK_ARG(ldc >= N && (ldc * cs) % 16 == 0, "proj_gemm: ldc must be >= N with 16-byte aligned rows");
+    MB_CHECK_ARG(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(C) % 16 == 0,
+                 "proj_gemm: pointers must be 16-byte aligned");
+    MB_CHECK_ARG(M <= (int64_t)0x7fffffff - 256, "proj_gemm: too many rows");
+    int dev = 0, major = 0;
+    MB_CUDA_TRY(cudaGetDevice(&dev));
+    MB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MB_CHECK_ARG(major == 10, "proj_gemm: needs a compute capability 10.x GPU (tcgen05)");
+    DevInfo info;
+    if (device_info(info)) return -1;
+
+    ProjParams p{};
+    p.bias = bias;
+    p.M = (int)M;
+    p.N = N;
+    p.K = K;
+    p.BN = N <= 256 ? (N + 15) / 16 * 16 : 256;
+    p.m_tiles = (int)((M + 255) / 256);
+    p.n_tiles = (N + p.BN - 1) / p.BN;
+    p.kblocks = (K + kPBK - 1) / kPBK;
+    p.mode = mode;
+    p.idesc = idesc_f16_f32acc(256, p.BN);
+    p.tx_bytes = (uint32_t)(2 * (kPStageA + (p.BN / 2) * kPBK * 2));
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+    MB_CHECK_ARG(tiles <= 0x7fffffff, "proj_gemm: too many tiles");
+
+    CUtensorMap ma, mw, mc;
+    const bool enc_ok =
+        encode_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, M, K, lda, kPBK, 128) &&
+        encode_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W, N, K, K, kPBK, p.BN / 2) &&
+        (mode == kProjF16 ? encode_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, M, N, ldc, 64, 32)
+                          : encode_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, M, N, ldc, 32, 32));
+    MB_CHECK_ARG(enc_ok, "proj_gemm: tensor map encoding failed");
+
+    const int pairs = (int)std::min<int64_t>(tiles, info.pairs);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kPThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPSmem;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    MB_CUDA_TRY(cudaLaunchKernelEx(&cfg, proj_gemm_kernel, ma, mw, mc, p));
+    return launch_status("projection GEMM (tcgen05, CTA pairs) kernel");
+}
+
+unsigned proj_error_flags(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_proj_error, sizeof(v)) != cudaSuccess) return ~0u;
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_proj_error, &z, sizeof(z));
+    }
+    return v;
+}
+
+}  // namespace mb

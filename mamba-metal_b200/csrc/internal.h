@@ -48,6 +48,13 @@ int gated_silu_mul(const void *gate, const void *up, void *out, int64_t n, int d
 int gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h, cudaStream_t st);
 unsigned gemm_error_flags(bool clear);
 
+// gemm_tc.cu
+enum ProjMode { kProjF16 = 0, kProjF32Add = 1, kProjF32 = 2 };
+int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void *C, int64_t ldc, int64_t M, int N,
+              int K, int mode, cudaStream_t st);
+constexpr int64_t kProjMinRows = 512;  // mamba_linear uses the CTA-pair GEMM above this many rows
+unsigned proj_error_flags(bool clear);
+
 // linear_tc.cu
 size_t linear_workspace_bytes(int64_t M, int N, int K);
 int linear_tc(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t M, int N,

@@ -346,7 +346,7 @@ int launch_bn(const CUtensorMap &mx, const CUtensorMap &mw, const LinearParams &
 }  // namespace
 
 size_t linear_workspace_bytes(int64_t M, int N, int K) {
-    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (M <= 0 || N <= 0 || K <= 0 || M > kProjMinRows) return 0;
     const Plan pl = make_plan(M, N, K, device_sm_count());
     if (pl.splits <= 1) return 0;
     return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
@@ -365,6 +365,8 @@ int linear_tc(const void *x, int64_t ldx, const void *w, const float *bias, void
                      reinterpret_cast<uintptr_t>(y) % 16 == 0,
                  "linear: pointers must be 16-byte aligned");
     MB_CHECK_ARG(M <= (int64_t)0x7fffffff - 256, "linear: too many rows");
+    // Many rows: the CTA-pair GEMM (gemm_tc.cu) without K splits.
+    if (M > kProjMinRows) return proj_gemm(x, ldx, w, bias, y, ldy, M, N, K, mode, st);
     int dev = 0, major = 0;
     MB_CUDA_TRY(cudaGetDevice(&dev));
     MB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));

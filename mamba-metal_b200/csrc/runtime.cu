@@ -150,7 +150,7 @@ struct OpScope {
     Profiler &p;
     int op;
     cudaStream_t st;
-    int kernels;
+    int kernels;  // this library's kernels in the operation (may be set after construction)
     cudaEvent_t a = nullptr;
     OpScope(Profiler &p_, int op_, cudaStream_t s, int k) : p(p_), op(op_), st(s), kernels(k) {
         if (p.on && (a = p.take())) cudaEventRecord(a, st);
@@ -256,6 +256,7 @@ struct Model {
         if (const char *g = std::getenv("MAMBA_STEP_GRAPH")) use_graphs = std::atoi(g) != 0;
         if (const char *t = std::getenv("MAMBA_TC_LINEAR")) tc_linear = std::atoi(t) != 0;
         if (const char *h = std::getenv("MAMBA_HOST_CHUNKS")) host_chunks = std::max(0, std::atoi(h));
+        if (const char *pj = std::getenv("MAMBA_PROJ")) proj_tc = std::atoi(pj) != 0;
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -301,7 +302,7 @@ struct Model {
     // tcgen05 linear kernel instead; at the decode shapes (256 rows) it is
     // measured 2-3x slower than cuBLAS (its K splits cannot balance the
     // output blocks over 148 SMs), so it is off by default.
-    static constexpr int64_t kTcRows = 512;
+    static constexpr int64_t kTcRows = kProjMinRows;
     bool tc_linear = false;  // read from MAMBA_TC_LINEAR when the model is created
     bool tc_linear_enabled() const { return tc_linear; }
     bool use_tc(int64_t rows, int n, int k, int lda, int ldc) const {
@@ -317,14 +318,32 @@ struct Model {
         return w;
     }
 
+    // FP16 projections of more than kTcRows rows (forward passes) run on this
+    // library's CTA-pair tcgen05 GEMM (gemm_tc.cu); MAMBA_PROJ=0 sends them
+    // to cuBLAS instead (for comparisons).
+    bool proj_tc = true;
+    int last_gemm_kernels = 0;  // this library's kernels launched by the last gemm()
+    bool use_proj(int64_t rows, int k, int lda, int ldc, int c_dtype) const {
+        return proj_tc && act == MAMBA_F16 && rows > kTcRows && k % 8 == 0 && lda % 8 == 0 &&
+               (ldc * (c_dtype == MAMBA_F16 ? 2 : 4)) % 16 == 0;
+    }
+
     int gemm(cudaStream_t st, int64_t rows, int n, int k, const void *A, int lda, const void *Wt,
              void *C, int ldc, int c_dtype, float beta, void *lws, size_t lws_bytes) {
+        last_gemm_kernels = 0;
         if (rows == 0 || n == 0) return 0;
         MB_CHECK_ARG(rows <= 0x7fffffffLL, "gemm: too many rows");
         const bool aligned = reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(Wt) % 16 == 0 &&
                              reinterpret_cast<uintptr_t>(C) % 16 == 0;
-        if (aligned && use_tc(rows, n, k, lda, ldc) && (beta == 0.f || (beta == 1.f && c_dtype == MAMBA_F32))) {
+        const bool beta_ok = beta == 0.f || (beta == 1.f && c_dtype == MAMBA_F32);
+        if (aligned && beta_ok && use_proj(rows, k, lda, ldc, c_dtype)) {
+            const int mode = c_dtype == MAMBA_F16 ? kProjF16 : (beta == 1.f ? kProjF32Add : kProjF32);
+            last_gemm_kernels = 1;
+            return proj_gemm(A, lda, Wt, nullptr, C, ldc, rows, n, k, mode, st);
+        }
+        if (aligned && use_tc(rows, n, k, lda, ldc) && beta_ok) {
             const int mode = c_dtype == MAMBA_F16 ? 0 : (beta == 1.f ? 1 : 2);
+            last_gemm_kernels = linear_workspace_bytes(rows, n, k) ? 2 : 1;
             return linear_tc(A, lda, Wt, nullptr, C, ldc, rows, n, k, mode, lws, lws_bytes, st);
         }
         const cudaDataType at = act == MAMBA_F16 ? CUDA_R_16F : CUDA_R_32F;
@@ -443,6 +462,7 @@ struct Model {
                 if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f, ar.lin_ws,
                          ar.lin_ws_bytes))
                     return -1;
+                o.kernels = last_gemm_kernels;
             }
             {
                 OpScope o(prof, MAMBA_OP_CONV, st, 1);
@@ -452,11 +472,13 @@ struct Model {
                 OpScope o(prof, MAMBA_OP_X_PROJ, st, 0);
                 if (gemm(st, T, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
                     return -1;
+                o.kernels = last_gemm_kernels;
             }
             {
                 OpScope o(prof, MAMBA_OP_DT_PROJ, st, 0);
                 if (gemm(st, T, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
                     return -1;
+                o.kernels = last_gemm_kernels;
             }
             {
                 MambaScanArgs sa = scan_args(w, ar, batch, L);
@@ -467,6 +489,7 @@ struct Model {
                 OpScope o(prof, MAMBA_OP_OUT_PROJ, st, 0);
                 if (gemm(st, T, M, D, ar.y, D, w.w_out_t, out, M, MAMBA_F32, 1.f, ar.lin_ws, ar.lin_ws_bytes))
                     return -1;
+                o.kernels = last_gemm_kernels;
             }
         }
         return 0;
@@ -647,6 +670,7 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
             if (m.gemm(st, Bt, 2 * D, m.M, ar.normed, m.M, w.w_in_t, ar.xz, 2 * D, m.act, 0.f, ar.lin_ws,
                        ar.lin_ws_bytes))
                 return -1;
+            o.kernels = m.last_gemm_kernels;
         }
         {
             OpScope o(pf, MAMBA_OP_CONV, st, 1);
@@ -658,11 +682,13 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
             OpScope o(pf, MAMBA_OP_X_PROJ, st, 0);
             if (m.gemm(st, Bt, XD, D, ar.u, D, w.w_x_t, ar.xdbc, XD, m.act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
                 return -1;
+            o.kernels = m.last_gemm_kernels;
         }
         {
             OpScope o(pf, MAMBA_OP_DT_PROJ, st, 0);
             if (m.gemm(st, Bt, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, m.act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
                 return -1;
+            o.kernels = m.last_gemm_kernels;
         }
         {
             OpScope o(pf, MAMBA_OP_SCAN, st, 1);
@@ -676,6 +702,7 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
             OpScope o(pf, MAMBA_OP_OUT_PROJ, st, 0);
             if (m.gemm(st, Bt, m.M, D, ar.y, D, w.w_out_t, out, m.M, MAMBA_F32, 1.f, ar.lin_ws, ar.lin_ws_bytes))
                 return -1;
+            o.kernels = m.last_gemm_kernels;
         }
     }
     return 0;
@@ -1030,7 +1057,8 @@ unsigned mamba_device_status(int clear) {
     const unsigned scan = mb::device_error_flags(clear != 0);
     const unsigned gemm = mb::gemm_error_flags(clear != 0);
     const unsigned lin = mb::linear_error_flags(clear != 0);
-    return (scan == ~0u || gemm == ~0u || lin == ~0u) ? ~0u : (scan | gemm | lin);
+    const unsigned proj = mb::proj_error_flags(clear != 0);
+    return (scan == ~0u || gemm == ~0u || lin == ~0u || proj == ~0u) ? ~0u : (scan | gemm | lin | proj);
 }
 
 int mamba_selftest_bounded_wait(unsigned limit_us, void *stream) {

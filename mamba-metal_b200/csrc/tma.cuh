@@ -1,6 +1,6 @@
 // tma.cuh -- shared-memory mbarrier and TMA (cp.async.bulk.tensor) helpers
-// for sm_100a, written directly in PTX.  No multicast form is used anywhere:
-// every bulk copy targets the issuing CTA's own shared memory.
+// for sm_100a, written directly in PTX.  Every bulk tensor load writes the
+// issuing CTA's own shared memory and reads this GPU's global memory.
 #pragma once
 
 #include <cuda.h>
@@ -94,5 +94,108 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+
+// ---- thread-block clusters (CTA pairs) -------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Full barrier across the CTAs of the cluster (release/acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile(
+        "barrier.cluster.arrive.release.aligned;\n"
+        "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address in the shared::cluster window of the variable at the same offset
+// in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Arrive (count 1) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Wait on a local barrier that other CTAs of the cluster also complete, with
+// cluster-scope acquire; bounded like mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t *bar, uint32_t parity,
+                                                          uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait_acq_cluster(bar, parity)) {
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
+// 2-D tiled bulk tensor load into this CTA's shared memory whose completion
+// (transaction bytes) is signalled on an mbarrier that may live in either
+// CTA of a CTA pair (`bar_cluster` is a shared::cluster address): the form
+// the pair-wide tensor-core pipelines use, where the leading CTA's barrier
+// counts the bytes of both CTAs' operand tiles.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+        : "memory");
+}
+
+// ---- bulk tensor stores (shared -> global) ---------------------------------
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tiled store of a shared-memory box to global memory (elements outside
+// the tensor are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+
+// 2-D tiled element-wise add of a shared-memory box into global memory
+// (the tensor map's element type; each element is added once, rounded once).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int c0, int c1) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N of this thread's committed bulk groups still read
+// shared memory (their sources may then be overwritten).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until all of this thread's committed bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 }  // namespace mb

@@ -34,7 +34,11 @@ SHAPES = [
     (256, 5120, 160),     # decode dt_proj: K tail (2.5 blocks)
     (300, 200, 136),      # two row tiles (the second ragged), ragged columns
     (1, 8, 8),            # smallest legal sizes
-    (8192, 1024, 128),    # 256 output blocks: no K split
+    (8192, 1024, 128),    # above 512 rows: the CTA-pair kernel
+    (4096, 8192, 2048),   # in_proj-like: 512 tiles over the persistent CTA pairs
+    (1000, 160, 4096),    # x_proj-like: one 160-column tile, ragged last row block
+    (777, 4096, 128),     # dt_proj-like: two K blocks per tile
+    (520, 200, 136),      # ragged columns (tile 208) and K tail, 8 rows in the last block
 ]
 
 
@@ -49,7 +53,8 @@ def test_linear_fp16_out(cuda, rows, n, k, bias):
     assert oracle.normwise_rel_err(y.float().cpu().numpy(), ref) < 2e-3
 
 
-@pytest.mark.parametrize("rows,n,k", [(256, 2560, 5120), (37, 64, 1024), (300, 200, 136)])
+@pytest.mark.parametrize("rows,n,k", [(256, 2560, 5120), (37, 64, 1024), (300, 200, 136), (600, 2048, 4096),
+                                      (1030, 96, 200)])
 def test_linear_fp32_accumulate_and_store(cuda, rows, n, k):
     """mode 1 adds into an FP32 buffer (the residual stream of out_proj);
     mode 2 overwrites it."""
@@ -103,3 +108,21 @@ def test_linear_rejects_bad_arguments(cuda):
     assert L.mamba_linear(x.data_ptr(), 5120, w.data_ptr(), None, y.data_ptr(), 192, 256, 192, 5120, 3, None, 0,
                           None) == -1
     assert "mode" in mb.last_error()
+
+
+def test_pair_gemm_strided_operand_and_determinism(cuda):
+    """Above 512 rows (the CTA-pair kernel): x read with a row stride wider
+    than K (dt_proj reads the first dt_rank columns of x_proj's output), and
+    repeated calls give identical bits."""
+    rows, n, k, ld = 2304, 4096, 128, 160
+    rng = np.random.default_rng(12)
+    full = rng.standard_normal((rows, ld)).astype(np.float16)
+    w = (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float16)
+    tx, tw = _dev(full), _dev(w)
+    ys = [mb.linear(tx[:, :k], tw, mode=0) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    ref = oracle.linear(full[:, :k], w)
+    assert oracle.normwise_rel_err(ys[0].float().cpu().numpy(), ref) < 2e-3
