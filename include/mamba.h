@@ -357,6 +357,25 @@ size_t mamba_linear_workspace(int64_t rows, int n, int k);
 int mamba_linear(const void *x, int64_t ldx, const void *w, const float *bias, void *y, int64_t ldy, int64_t rows,
                  int n, int k, int mode, void *workspace, size_t workspace_bytes, void *stream);
 
+/* in_proj with the causal conv fused into its epilogue (the first three
+ * steps of the layer graph after RMSNorm, MambaRuntime.cpp:94-96:
+ * linear_f16, projection.metal:32-49, then causal_conv1d_f16 + SiLU,
+ * causal_conv1d.metal:85-100, on its x half), one tensor-core kernel:
+ *   xz = x @ w_in^T (FP32 accumulation, rounded to FP16),
+ *   u  = SiLU(conv(xz[:, :d_inner]) + conv_b),   z = xz[:, d_inner:]
+ * where the conv is causal along each sequence of `seqlen` tokens (zero
+ * before its start), taps oldest first.  x FP16 [batch*seqlen, d_model];
+ * w_in FP16 [2*d_inner, d_model] (in_proj transposed); conv_w FP32
+ * [d_inner, 4]; conv_b FP32 [d_inner]; u FP16 [batch*seqlen, d_inner];
+ * z FP16 rows of z_row_stride elements (the x half of xz is never written).
+ * Requires d_conv = 4, d_inner a multiple of 256, d_model a multiple of 8,
+ * 16-byte aligned pointers, a compute capability 10.x GPU.  Results equal
+ * mamba_linear (mode 0) followed by mamba_causal_conv1d (silu = 1) bit for
+ * bit.  0 / -1. */
+int mamba_in_proj_conv(const void *x, const void *w_in, const float *conv_w, const float *conv_b, void *u, void *z,
+                       int64_t z_row_stride, int batch, int seqlen, int d_model, int d_inner, int d_conv,
+                       void *stream);
+
 /* Fused SwiGLU up-projection on the tensor cores (no reference
  * counterpart as one op: the reference's linear_f16 twice, then
  * gated_silu_mul_f16, gated_mlp.metal:12-41):

@@ -43,6 +43,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "scan_math.cuh"
 #include "tma.cuh"
 #include "umma.cuh"
 
@@ -63,15 +64,21 @@ constexpr int kPStageB = 128 * kPBK * 2;          // 16 KB: up to 128 rows of W
 constexpr int kPStage = kPStageA + kPStageB;
 constexpr int kPEpiBox = 32 * 128;                // 4 KB: 32 rows x 128 bytes
 constexpr int kPEpiBytes = 4 * 2 * kPEpiBox;      // 4 warps x 2 buffers
-constexpr int kPSmem = kPStages * kPStage + kPEpiBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int kPXPitch = 68;                      // bytes per row of the conv input tile (32 FP16 + pad)
+constexpr int kPXchBytes = 2 * 128 * kPXPitch;    // conv input tile [128 rows][32 cols] FP16, double-buffered
+constexpr int kPSmem = kPStages * kPStage + kPEpiBytes + kPXchBytes + 1024 /* alignment */ + 256 /* barriers */;
 constexpr unsigned kErrProjTimeout = 16u;
 
 struct ProjParams {
-    const float *bias;  // [N] FP32 added to every row, or NULL
+    const float *bias;              // [N] FP32 added to every row, or NULL
+    const float *conv_w, *conv_b;   // conv-fused in_proj: [D, 4] and [D] FP32
     int M, N, K;
     int BN;          // output columns per tile (multiple of 16, <= 256)
     int m_tiles, n_tiles, kblocks;
     int mode;
+    int halo;        // rows each CTA computes ahead of its first output row (3 when the conv is fused)
+    int L;           // conv-fused: sequence length (the conv restarts at every multiple of L)
+    int x_tiles;     // conv-fused: column tiles 0..x_tiles-1 hold the conv input x, the rest z
     uint32_t idesc;
     uint32_t tx_bytes;  // operand bytes of one stage, both CTAs
 };
@@ -86,6 +93,10 @@ __device__ __forceinline__ uint32_t pack_half2(uint32_t a, uint32_t b) {
     const __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
     return *reinterpret_cast<const uint32_t *>(&h);
 }
+__device__ __forceinline__ uint32_t pack_half2f(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
 
 // Row `r` of a 32-row box of 128-byte rows with the TMA 128-byte swizzle:
 // 16-byte chunk j lands at chunk j ^ (r % 8).
@@ -93,13 +104,45 @@ __device__ __forceinline__ void st_swizzled(uint8_t *box, int r, int j, uint4 v)
     *reinterpret_cast<uint4 *>(box + r * 128 + ((j ^ (r & 7)) << 4)) = v;
 }
 
+// The four epilogue warps (threads 64..191) synchronise among themselves.
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Same barrier, returning whether `ok` holds in every epilogue thread, so
+// that the warps leave their tile loop together (a warp that left alone
+// would strand the others at the next barrier).
+__device__ __forceinline__ bool epilogue_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n"
+        " .reg .pred p, q;\n"
+        " setp.ne.u32 p, %1, 0;\n"
+        " bar.red.and.pred q, 1, 128, p;\n"
+        " selp.u32 %0, 1, 0, q;\n"
+        "}\n"
+        : "=r"(r)
+        : "r"((uint32_t)ok)
+        : "memory");
+    return r != 0;
+}
+
+// FP16 element (r, cc) of a 32-row box of 128-byte rows with the TMA
+// 128-byte swizzle (cc < 64).
+__device__ __forceinline__ void st_swizzled_h(uint8_t *box, int r, int cc, float v) {
+    *reinterpret_cast<__half *>(box + r * 128 + ((((cc >> 3) ^ (r & 7))) << 4) + ((cc & 7) << 1)) =
+        __float2half_rn(v);
+}
+
+template <bool CONV>
 __global__ void __launch_bounds__(kPThreads, 1)
     proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_c, const ProjParams p) {
+                     const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c_short,
+                     const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_z_short,
+                     const ProjParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *epi = smem + kPStages * kPStage;
-    uint64_t *full = reinterpret_cast<uint64_t *>(epi + kPEpiBytes);
+    uint8_t *xch = epi + kPEpiBytes;  // conv input tiles
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi + kPEpiBytes + kPXchBytes);
     uint64_t *empty = full + kPStages;
     uint64_t *tfull = empty + kPStages;
     uint64_t *tempty = tfull + 2;
@@ -110,6 +153,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles = p.m_tiles * p.n_tiles;
+    // Row geometry: a CTA computes 128 rows starting `halo` rows before its
+    // first output row; a pair advances by 2 * (128 - halo) rows per tile.
+    const int rstep = 128 - p.halo;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPStages; ++s) {
@@ -143,7 +189,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
             uint32_t it = 0;
             for (int tile = pair; tile < tiles && ok; tile += npairs) {
                 const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-                const int arow = mt * 256 + (int)rank * 128, brow = nt * p.BN + (int)rank * half;
+                // may be negative for the first tile (the halo): those rows read zeros
+                const int arow = mt * 2 * rstep + (int)rank * rstep - p.halo;
+                const int brow = nt * p.BN + (int)rank * half;
                 for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
                     const uint32_t s = it % kPStages, ph = (it / kPStages) & 1;
                     if (!mbar_wait_bounded(&empty[s], ph ^ 1)) {
@@ -198,73 +246,155 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else {
         // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows
-        // 32*(w%4) .. +31 of this CTA's 128.
+        // 32*(w%4) .. +31 of this CTA's 128.  In the first quarter the rows
+        // before `halo` are not outputs: that warp stores a shorter box
+        // (map *_short) from shared-memory row 0 = tile row `halo`.
         const int quarter = warp & 3;
+        const int skip = quarter == 0 ? p.halo : 0;
+        const int srow = lane - skip;  // this lane's row in the staged box (< 0: not stored)
         uint8_t *boxes = epi + (warp - 2) * 2 * kPEpiBox;
         const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
         const bool f16 = p.mode == kProjF16;
         const int cstep = f16 ? 64 : 32;
-        uint32_t tcount = 0, nbox = 0;
+        uint32_t tcount = 0, nbox = 0, nchunk = 0;
         for (int tile = pair; tile < tiles; tile += npairs, ++tcount) {
             const uint32_t b = tcount & 1, tph = (tcount >> 1) & 1;
-            if (!warp_wait_p(&tfull[b], tph)) {
+            bool have = warp_wait_p(&tfull[b], tph);
+            if (CONV) have = epilogue_all(have);
+            if (!have) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-            const int row0 = mt * 256 + (int)rank * 128 + quarter * 32;
+            const int wrow = mt * 2 * rstep + (int)rank * rstep - p.halo + quarter * 32;  // this warp's first row
+            const int out_row = wrow + skip;                                                // first stored row
+            const bool conv_tile = CONV && nt < p.x_tiles;
+            const int ncol = CONV ? (conv_tile ? nt : nt - p.x_tiles) * p.BN : nt * p.BN;
+            const CUtensorMap *mfull = (CONV && !conv_tile) ? &map_z : &map_c;
+            const CUtensorMap *mshort = (CONV && !conv_tile) ? &map_z_short : &map_c_short;
+            const CUtensorMap *mstore = skip ? mshort : mfull;
+            const int ncols = CONV ? p.N / 2 : p.N;  // columns of the tensor being stored
+            // sequence position of this warp's first row (the conv restarts
+            // at t = 0; halo rows before the first token count as t < 0)
+            int tpos0 = 0;
+            if (conv_tile) tpos0 = ((wrow % p.L) + p.L) % p.L;
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + b * kPAccCols;
             for (int c = 0; c < p.BN; c += cstep) {
-                const int col = nt * p.BN + c;
-                uint32_t v0[32], v1[32];
-                tmem_ld_32x32b_x32(tl + c, v0);
-                if (f16) tmem_ld_32x32b_x32(tl + c + 32, v1);
-                tmem_wait_ld();
-                if (col >= p.N || row0 >= p.M) continue;  // nothing of this box is inside C
-                if (p.bias) {
-                    // every lane reads the same bias entries (broadcast loads)
+                const int col = ncol + c;
+                uint32_t v0[32];
+                uint32_t pk[32];  // FP16 output: 64 columns as 32 packed pairs
+                if (CONV && conv_tile) {
+                    // Causal conv (width 4) + bias + SiLU, the arithmetic of the
+                    // library's conv kernel (conv.cu), on two 32-column halves.
+                    // Each warp writes its 32 rows of FP16-rounded x (the values
+                    // the unfused path stores) into a shared tile; then lane l
+                    // walks column l down the warp's rows with a 3-row window
+                    // that starts in the previous warp's rows and restarts at
+                    // every sequence start.  Taps oldest first, fma, then the
+                    // bias, as conv.cu does.
+                    uint8_t *box = boxes + (nbox & 1) * kPEpiBox;
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+#pragma unroll 1
+                    for (int hlf = 0; hlf < 2; ++hlf) {
+                        tmem_ld_32x32b_x32(tl + c + 32 * hlf, v0);
+                        tmem_wait_ld();
+                        uint8_t *X = xch + (nchunk & 1) * (128 * kPXPitch);
+                        uint8_t *xrow = X + (quarter * 32 + lane) * kPXPitch;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col + j < p.N) v0[j] = __float_as_uint(__uint_as_float(v0[j]) + p.bias[col + j]);
+                        for (int j = 0; j < 16; ++j)
+                            *reinterpret_cast<uint32_t *>(xrow + 4 * j) = pack_half2(v0[2 * j], v0[2 * j + 1]);
+                        epilogue_bar();
+                        const int cc = col + 32 * hlf + lane;  // this lane's channel
+                        const float4 wv = __ldg(reinterpret_cast<const float4 *>(p.conv_w) + min(cc, ncols - 1));
+                        const float bj = __ldg(p.conv_b + min(cc, ncols - 1));
+                        const __half *xc = reinterpret_cast<const __half *>(X) + lane;  // column `lane`, row stride 34
+                        // window rows 32q-3 .. 32q-1, zero before the sequence start
+                        float w0 = 0.f, w1 = 0.f, w2 = 0.f;
+                        if (quarter > 0) {
+                            const int r0 = quarter * 32;
+                            if (tpos0 >= 3) w0 = __half2float(xc[(r0 - 3) * (kPXPitch / 2)]);
+                            if (tpos0 >= 2) w1 = __half2float(xc[(r0 - 2) * (kPXPitch / 2)]);
+                            if (tpos0 >= 1) w2 = __half2float(xc[(r0 - 1) * (kPXPitch / 2)]);
+                        }
+                        int t = tpos0;
+#pragma unroll 8
+                        for (int i = 0; i < 32; ++i) {
+                            const float x3 = __half2float(xc[(quarter * 32 + i) * (kPXPitch / 2)]);
+                            if (t == 0) w0 = w1 = w2 = 0.f;
+                            float acc = fmaf(w0, wv.x, 0.f);
+                            acc = fmaf(w1, wv.y, acc);
+                            acc = fmaf(w2, wv.z, acc);
+                            acc = fmaf(x3, wv.w, acc);
+                            acc += bj;
+                            const int sr = i - skip;
+                            if (sr >= 0) st_swizzled_h(box, sr, 32 * hlf + lane, silu_fast(acc));
+                            w0 = w1;
+                            w1 = w2;
+                            w2 = x3;
+                            t = (t + 1 == p.L) ? 0 : t + 1;
+                        }
+                        ++nchunk;
+                    }
+                    if (col >= ncols || out_row >= p.M) continue;
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(mstore, box, col, out_row);
+                        bulk_commit_group();
+                    }
+                    ++nbox;
+                    continue;
+                } else {
+                    uint32_t v1[32];
+                    tmem_ld_32x32b_x32(tl + c, v0);
+                    if (f16) tmem_ld_32x32b_x32(tl + c + 32, v1);
+                    tmem_wait_ld();
                     if (f16) {
+                        if (p.bias) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                if (col + j < ncols)
+                                    v0[j] = __float_as_uint(__uint_as_float(v0[j]) + p.bias[col + j]);
+                                if (col + 32 + j < ncols)
+                                    v1[j] = __float_as_uint(__uint_as_float(v1[j]) + p.bias[col + 32 + j]);
+                            }
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            pk[j] = pack_half2(v0[2 * j], v0[2 * j + 1]);
+                            pk[16 + j] = pack_half2(v1[2 * j], v1[2 * j + 1]);
+                        }
+                    } else if (p.bias) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (col + 32 + j < p.N)
-                                v1[j] = __float_as_uint(__uint_as_float(v1[j]) + p.bias[col + 32 + j]);
+                            if (col + j < ncols) v0[j] = __float_as_uint(__uint_as_float(v0[j]) + p.bias[col + j]);
                     }
                 }
+                if (col >= ncols || out_row >= p.M) continue;  // nothing of this box is inside C
                 uint8_t *box = boxes + (nbox & 1) * kPEpiBox;
                 // the bulk store that last read this box has finished reading it
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();
-                if (f16) {
+                if (srow >= 0) {
+                    if (f16) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        st_swizzled(box, lane, j,
-                                    make_uint4(pack_half2(v0[8 * j], v0[8 * j + 1]),
-                                               pack_half2(v0[8 * j + 2], v0[8 * j + 3]),
-                                               pack_half2(v0[8 * j + 4], v0[8 * j + 5]),
-                                               pack_half2(v0[8 * j + 6], v0[8 * j + 7])));
+                        for (int j = 0; j < 8; ++j)
+                            st_swizzled(box, srow, j, make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        st_swizzled(box, lane, 4 + j,
-                                    make_uint4(pack_half2(v1[8 * j], v1[8 * j + 1]),
-                                               pack_half2(v1[8 * j + 2], v1[8 * j + 3]),
-                                               pack_half2(v1[8 * j + 4], v1[8 * j + 5]),
-                                               pack_half2(v1[8 * j + 6], v1[8 * j + 7])));
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        st_swizzled(box, lane, j, make_uint4(v0[4 * j], v0[4 * j + 1], v0[4 * j + 2], v0[4 * j + 3]));
+                        for (int j = 0; j < 8; ++j)
+                            st_swizzled(box, srow, j, make_uint4(v0[4 * j], v0[4 * j + 1], v0[4 * j + 2], v0[4 * j + 3]));
+                    }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     if (p.mode == kProjF32Add)
-                        tma_reduce_add_2d(&map_c, box, col, row0);
+                        tma_reduce_add_2d(mstore, box, col, out_row);
                     else
-                        tma_store_2d(&map_c, box, col, row0);
+                        tma_store_2d(mstore, box, col, out_row);
                     bulk_commit_group();
                 }
                 ++nbox;
@@ -314,6 +444,7 @@ struct DevInfo {
     int pairs = 0;
 };
 
+template <bool CONV>
 int device_info(DevInfo &out) {
     static std::mutex mu;
     static std::vector<DevInfo> cache;
@@ -323,7 +454,8 @@ int device_info(DevInfo &out) {
     if ((int)cache.size() <= dev) cache.resize(dev + 1);
     DevInfo &d = cache[dev];
     if (!d.ready) {
-        MB_CUDA_TRY(cudaFuncSetAttribute(proj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
+        MB_CUDA_TRY(
+            cudaFuncSetAttribute(proj_gemm_kernel<CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
         cudaLaunchConfig_t cfg{};
         cudaLaunchAttribute attr{};
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -336,13 +468,45 @@ int device_info(DevInfo &out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        MB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, proj_gemm_kernel, &cfg));
+        MB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, proj_gemm_kernel<CONV>, &cfg));
         MB_CHECK_ARG(n > 0, "proj_gemm: no CTA pair fits on this GPU");
         d.pairs = n;
         d.ready = true;
     }
     out = d;
     return 0;
+}
+
+int check_tc_device(const char *what) {
+    int dev = 0, major = 0;
+    MB_CUDA_TRY(cudaGetDevice(&dev));
+    MB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MB_CHECK_ARG(major == 10, std::string(what) + ": needs a compute capability 10.x GPU (tcgen05)");
+    return 0;
+}
+
+template <bool CONV>
+int launch_proj(const CUtensorMap *maps, const ProjParams &p, cudaStream_t st) {
+    DevInfo info;
+    if (device_info<CONV>(info)) return -1;
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+    MB_CHECK_ARG(tiles <= 0x7fffffff, "proj_gemm: too many tiles");
+    const int pairs = (int)std::min<int64_t>(tiles, info.pairs);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kPThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPSmem;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    MB_CUDA_TRY(cudaLaunchKernelEx(&cfg, proj_gemm_kernel<CONV>, maps[0], maps[1], maps[2], maps[3], maps[4],
+                                   maps[5], p));
+    return launch_status("projection GEMM (tcgen05, CTA pairs) kernel");
 }
 
 }  // namespace
@@ -360,12 +524,7 @@ int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void
                      reinterpret_cast<uintptr_t>(C) % 16 == 0,
                  "proj_gemm: pointers must be 16-byte aligned");
     MB_CHECK_ARG(M <= (int64_t)0x7fffffff - 256, "proj_gemm: too many rows");
-    int dev = 0, major = 0;
-    MB_CUDA_TRY(cudaGetDevice(&dev));
-    MB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
-    MB_CHECK_ARG(major == 10, "proj_gemm: needs a compute capability 10.x GPU (tcgen05)");
-    DevInfo info;
-    if (device_info(info)) return -1;
+    if (check_tc_device("proj_gemm")) return -1;
 
     ProjParams p{};
     p.bias = bias;
@@ -377,34 +536,65 @@ int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void
     p.n_tiles = (N + p.BN - 1) / p.BN;
     p.kblocks = (K + kPBK - 1) / kPBK;
     p.mode = mode;
+    p.halo = 0;
     p.idesc = idesc_f16_f32acc(256, p.BN);
     p.tx_bytes = (uint32_t)(2 * (kPStageA + (p.BN / 2) * kPBK * 2));
-    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
-    MB_CHECK_ARG(tiles <= 0x7fffffff, "proj_gemm: too many tiles");
 
-    CUtensorMap ma, mw, mc;
+    CUtensorMap maps[6];
     const bool enc_ok =
-        encode_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, M, K, lda, kPBK, 128) &&
-        encode_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W, N, K, K, kPBK, p.BN / 2) &&
-        (mode == kProjF16 ? encode_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, M, N, ldc, 64, 32)
-                          : encode_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, M, N, ldc, 32, 32));
+        encode_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, M, K, lda, kPBK, 128) &&
+        encode_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W, N, K, K, kPBK, p.BN / 2) &&
+        (mode == kProjF16 ? encode_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, M, N, ldc, 64, 32)
+                          : encode_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, M, N, ldc, 32, 32));
     MB_CHECK_ARG(enc_ok, "proj_gemm: tensor map encoding failed");
+    maps[3] = maps[4] = maps[5] = maps[2];  // no halo, no second output
+    return launch_proj<false>(maps, p, st);
+}
 
-    const int pairs = (int)std::min<int64_t>(tiles, info.pairs);
-    cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr{};
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kPThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPSmem;
-    cfg.stream = st;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    MB_CUDA_TRY(cudaLaunchKernelEx(&cfg, proj_gemm_kernel, ma, mw, mc, p));
-    return launch_status("projection GEMM (tcgen05, CTA pairs) kernel");
+bool proj_conv_supported(int64_t T, int L, int D, int Mdim, int K) {
+    return K == 4 && D % 256 == 0 && Mdim % 8 == 0 && L > 0 && T > 0 && T % L == 0 && T <= 0x7fff0000LL;
+}
+
+int proj_gemm_conv(const void *A, const void *W, const float *conv_w, const float *conv_b, void *u, void *z,
+                   int64_t ldz, int64_t T, int L, int D, int Mdim, int K, cudaStream_t st) {
+    MB_CHECK_ARG(T >= 0, "proj_gemm_conv: bad sizes");
+    if (T == 0) return 0;
+    MB_CHECK_ARG(A && W && conv_w && conv_b && u && z, "proj_gemm_conv: null pointer");
+    MB_CHECK_ARG(proj_conv_supported(T, L, D, Mdim, K),
+                 "proj_gemm_conv: needs d_conv 4, d_inner a multiple of 256, d_model a multiple of 8");
+    MB_CHECK_ARG(ldz >= D && ldz % 8 == 0, "proj_gemm_conv: z row stride");
+    MB_CHECK_ARG(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(u) % 16 == 0 && reinterpret_cast<uintptr_t>(z) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(conv_w) % 16 == 0,
+                 "proj_gemm_conv: pointers must be 16-byte aligned");
+    if (check_tc_device("proj_gemm_conv")) return -1;
+    const int halo = K - 1;
+    ProjParams p{};
+    p.conv_w = conv_w;
+    p.conv_b = conv_b;
+    p.M = (int)T;
+    p.N = 2 * D;
+    p.K = Mdim;
+    p.BN = 256;
+    p.m_tiles = (int)((T + 2 * (128 - halo) - 1) / (2 * (128 - halo)));
+    p.n_tiles = 2 * D / p.BN;
+    p.kblocks = (Mdim + kPBK - 1) / kPBK;
+    p.mode = kProjF16;
+    p.halo = halo;
+    p.L = L;
+    p.x_tiles = D / p.BN;
+    p.idesc = idesc_f16_f32acc(256, p.BN);
+    p.tx_bytes = (uint32_t)(2 * (kPStageA + (p.BN / 2) * kPBK * 2));
+    CUtensorMap maps[6];
+    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const bool enc_ok = encode_2d(&maps[0], F16, 2, A, T, Mdim, Mdim, kPBK, 128) &&
+                        encode_2d(&maps[1], F16, 2, W, 2 * (int64_t)D, Mdim, Mdim, kPBK, p.BN / 2) &&
+                        encode_2d(&maps[2], F16, 2, u, T, D, D, 64, 32) &&
+                        encode_2d(&maps[3], F16, 2, u, T, D, D, 64, 32 - halo) &&
+                        encode_2d(&maps[4], F16, 2, z, T, D, ldz, 64, 32) &&
+                        encode_2d(&maps[5], F16, 2, z, T, D, ldz, 64, 32 - halo);
+    MB_CHECK_ARG(enc_ok, "proj_gemm_conv: tensor map encoding failed");
+    return launch_proj<true>(maps, p, st);
 }
 
 unsigned proj_error_flags(bool clear) {

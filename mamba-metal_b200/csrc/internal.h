@@ -53,6 +53,12 @@ enum ProjMode { kProjF16 = 0, kProjF32Add = 1, kProjF32 = 2 };
 int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void *C, int64_t ldc, int64_t M, int N,
               int K, int mode, cudaStream_t st);
 constexpr int64_t kProjMinRows = 512;  // mamba_linear uses the CTA-pair GEMM above this many rows
+// in_proj with the causal conv + SiLU fused into its epilogue:
+// u = SiLU(conv(x)) [T, D] and z [T, D] (row stride ldz) from A [T, Mdim]
+// and W = in_proj^T [2D, Mdim]; T = batch * L tokens, sequences of L.
+bool proj_conv_supported(int64_t T, int L, int D, int Mdim, int K);
+int proj_gemm_conv(const void *A, const void *W, const float *conv_w, const float *conv_b, void *u, void *z,
+                   int64_t ldz, int64_t T, int L, int D, int Mdim, int K, cudaStream_t st);
 unsigned proj_error_flags(bool clear);
 
 // linear_tc.cu

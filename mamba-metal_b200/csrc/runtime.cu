@@ -257,6 +257,7 @@ struct Model {
         if (const char *t = std::getenv("MAMBA_TC_LINEAR")) tc_linear = std::atoi(t) != 0;
         if (const char *h = std::getenv("MAMBA_HOST_CHUNKS")) host_chunks = std::max(0, std::atoi(h));
         if (const char *pj = std::getenv("MAMBA_PROJ")) proj_tc = std::atoi(pj) != 0;
+        if (const char *cf = std::getenv("MAMBA_CONV_FUSE")) conv_fuse = std::atoi(cf) != 0;
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -323,6 +324,13 @@ struct Model {
     // to cuBLAS instead (for comparisons).
     bool proj_tc = true;
     int last_gemm_kernels = 0;  // this library's kernels launched by the last gemm()
+    // in_proj and the causal conv as one kernel (MAMBA_CONV_FUSE=0 keeps
+    // them separate, e.g. for comparisons); needs the FP16 CTA-pair GEMM.
+    bool conv_fuse = true;
+    bool fuse_conv(int64_t T, int L) const {
+        return conv_fuse && proj_tc && act == MAMBA_F16 && T > kTcRows && proj_conv_supported(T, L, D, M, K);
+    }
+
     bool use_proj(int64_t rows, int k, int lda, int ldc, int c_dtype) const {
         return proj_tc && act == MAMBA_F16 && rows > kTcRows && k % 8 == 0 && lda % 8 == 0 &&
                (ldc * (c_dtype == MAMBA_F16 ? 2 : 4)) % 16 == 0;
@@ -457,16 +465,26 @@ struct Model {
                 OpScope o(prof, MAMBA_OP_RMSNORM, st, 1);
                 if (rmsnorm(out, w.norm_w, ar.normed, T, M, kNormEps, MAMBA_F32, act, st)) return -1;
             }
-            {
-                OpScope o(prof, MAMBA_OP_IN_PROJ, st, 0);
-                if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f, ar.lin_ws,
-                         ar.lin_ws_bytes))
+            if (fuse_conv(T, L)) {
+                // in_proj with the causal conv + SiLU in its epilogue: writes
+                // u and the z half of xz; the x half is never stored.
+                OpScope o(prof, MAMBA_OP_IN_PROJ, st, 1);
+                if (proj_gemm_conv(ar.normed, w.w_in_t, w.conv_w, w.conv_b, ar.u,
+                                   static_cast<char *>(ar.xz) + (size_t)D * act_size(), 2 * D, T, L, D, M, K, st))
                     return -1;
-                o.kernels = last_gemm_kernels;
-            }
-            {
-                OpScope o(prof, MAMBA_OP_CONV, st, 1);
-                if (causal_conv1d(ar.xz, xs, w.conv_w, w.conv_b, ar.u, us, batch, L, D, K, 1, act, st)) return -1;
+            } else {
+                {
+                    OpScope o(prof, MAMBA_OP_IN_PROJ, st, 0);
+                    if (gemm(st, T, 2 * D, M, ar.normed, M, w.w_in_t, ar.xz, 2 * D, act, 0.f, ar.lin_ws,
+                             ar.lin_ws_bytes))
+                        return -1;
+                    o.kernels = last_gemm_kernels;
+                }
+                {
+                    OpScope o(prof, MAMBA_OP_CONV, st, 1);
+                    if (causal_conv1d(ar.xz, xs, w.conv_w, w.conv_b, ar.u, us, batch, L, D, K, 1, act, st))
+                        return -1;
+                }
             }
             {
                 OpScope o(prof, MAMBA_OP_X_PROJ, st, 0);
@@ -1262,6 +1280,22 @@ int mamba_linear(const void *x, int64_t ldx, const void *w, const float *bias, v
     mb::clear_error();
     return mb::linear_tc(x, ldx, w, bias, y, ldy, rows, n, k, mode, workspace, workspace_bytes,
                          static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
+}
+
+int mamba_in_proj_conv(const void *x, const void *w_in, const float *conv_w, const float *conv_b, void *u, void *z,
+                       int64_t z_row_stride, int batch, int seqlen, int d_model, int d_inner, int d_conv,
+                       void *stream) {
+    mb::clear_error();
+    if (batch < 0 || seqlen < 0) {
+        set_error("mamba_in_proj_conv: negative batch or seqlen");
+        return -1;
+    }
+    const int64_t T = (int64_t)batch * seqlen;
+    if (T == 0) return 0;
+    return mb::proj_gemm_conv(x, w_in, conv_w, conv_b, u, z, z_row_stride, T, seqlen, d_inner, d_model, d_conv,
+                              static_cast<cudaStream_t>(stream))
                ? -1
                : 0;
 }

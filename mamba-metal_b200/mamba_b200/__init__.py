@@ -114,6 +114,8 @@ _PROTOTYPES = {
     "mamba_propagate_tile_carries": (c_int, [c_void_p, c_int, c_i64, c_void_p, c_void_p]),
     "mamba_gated_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_void_p]),
     "mamba_gated_mlp_up": (c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int, c_void_p]),
+    "mamba_in_proj_conv": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int,
+                                   c_int, c_int, c_int, c_void_p]),
     "mamba_linear_workspace": (c_size, [c_i64, c_int, c_int]),
     "mamba_selftest_bounded_wait": (c_int, [ctypes.c_uint, c_void_p]),
     "mamba_linear": (c_int, [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_int, c_int, c_int,
@@ -579,6 +581,25 @@ def linear(x, w, bias=None, y=None, mode=0, workspace=None, stream=None):
     _check(lib().mamba_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), rows, n, k, mode,
                               ws_ptr, ws_len, _stream(stream)), "mamba_linear")
     return y
+
+
+def in_proj_conv(x, w_in, conv_w, conv_b, batch, seqlen, u=None, z=None, stream=None):
+    """in_proj with the causal conv + SiLU fused (mamba_in_proj_conv).
+    x FP16 [batch*seqlen, d_model]; w_in FP16 [2*d_inner, d_model]; conv_w
+    FP32 [d_inner, 4]; conv_b FP32 [d_inner].  Returns (u, z), FP16
+    [batch*seqlen, d_inner] each (z may be a strided view)."""
+    torch = _torch()
+    T, dm = x.shape
+    D = w_in.shape[0] // 2
+    assert x.is_contiguous() and w_in.is_contiguous() and T == batch * seqlen
+    if u is None:
+        u = torch.empty((T, D), dtype=torch.float16, device=x.device)
+    if z is None:
+        z = torch.empty((T, D), dtype=torch.float16, device=x.device)
+    assert z.stride(1) == 1
+    _check(lib().mamba_in_proj_conv(_ptr(x), _ptr(w_in), _ptr(conv_w), _ptr(conv_b), _ptr(u), _ptr(z), z.stride(0),
+                                    batch, seqlen, dm, D, conv_w.shape[1], _stream(stream)), "mamba_in_proj_conv")
+    return u, z
 
 
 def gated_mlp_up(x, w_gate_up, out=None, stream=None):

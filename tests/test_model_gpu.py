@@ -254,3 +254,23 @@ def test_save_weights_round_trip(cuda):
     assert np.array_equal(w, w.astype(np.float16).astype(np.float32))
     assert mb.lib().mamba_save_weights(a.handle, blob.ctypes.data, blob.nbytes - 4) == -1
     assert "size" in mb.last_error()
+
+
+def test_fused_conv_forward_equals_unfused(cuda, monkeypatch):
+    """The forward with in_proj and the causal conv fused in one kernel gives
+    the same bits as the forward with them separate (MAMBA_CONV_FUSE=0)."""
+    rng = np.random.default_rng(110)
+    cfg = mb.MambaConfig(128, 16, 4, 2, 2, mb.F16)
+    layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
+    blob = mb.make_weight_blob(cfg, layers)
+    monkeypatch.setenv("MAMBA_CONV_FUSE", "0")
+    sep = mb.Model(128, 16, 4, 2, 2, mb.F16)
+    monkeypatch.setenv("MAMBA_CONV_FUSE", "1")
+    fused = mb.Model(128, 16, 4, 2, 2, mb.F16)
+    sep.load_weights(blob)
+    fused.load_weights(blob)
+    h = rng.standard_normal((3, 333, 128)).astype(np.float32)
+    a, b = sep.forward(h), fused.forward(h)
+    assert np.array_equal(a, b)
+    ref = block_ref.model_forward(h, layers, cfg, block_ref.F16)
+    assert oracle.normwise_rel_err(b - h, ref - h) < 2e-3
