@@ -125,11 +125,36 @@ __device__ __forceinline__ bool epilogue_all(bool ok) {
     return r != 0;
 }
 
-// FP16 element (r, cc) of a 32-row box of 128-byte rows with the TMA
-// 128-byte swizzle (cc < 64).
-__device__ __forceinline__ void st_swizzled_h(uint8_t *box, int r, int cc, float v) {
-    *reinterpret_cast<__half *>(box + r * 128 + ((((cc >> 3) ^ (r & 7))) << 4) + ((cc & 7) << 1)) =
-        __float2half_rn(v);
+// Conv (width 4) + bias + SiLU down one column of 32 rows of the shared
+// FP16 tile (element (r, col) at xc[r * kPXPitch / 2]), rows r0 .. r0+31,
+// window (w0, w1, w2) = the three rows before r0; the FP16 result of row i
+// goes to row (i - SKIP) & 31 of the 128-byte-swizzled output box (rows
+// SKIP-1 .. below 0 wrap to rows the store never reads).  `off[k]` is this
+// lane's byte offset within a box row whose swizzle phase is k.  FAST: no
+// sequence starts inside the window; otherwise the window restarts (zeros)
+// at every row whose sequence position t is 0.
+template <int SKIP, bool FAST>
+__device__ __forceinline__ void conv_column(const __half *__restrict__ xc, int r0, float w0, float w1, float w2,
+                                            const float4 wv, float bj, uint8_t *box, const uint32_t (&off)[8], int t,
+                                            int L) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float x3 = __half2float(xc[(r0 + i) * (kPXPitch / 2)]);
+        if (!FAST) {
+            if (t == 0) w0 = w1 = w2 = 0.f;
+            t = (t + 1 == L) ? 0 : t + 1;
+        }
+        float acc = fmaf(w0, wv.x, 0.f);
+        acc = fmaf(w1, wv.y, acc);
+        acc = fmaf(w2, wv.z, acc);
+        acc = fmaf(x3, wv.w, acc);
+        acc += bj;
+        const int sr = (i - SKIP) & 31;
+        *reinterpret_cast<__half *>(box + sr * 128 + off[sr & 7]) = __float2half_rn(silu_fast(acc));
+        w0 = w1;
+        w1 = w2;
+        w2 = x3;
+    }
 }
 
 template <bool CONV>
@@ -279,6 +304,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // at t = 0; halo rows before the first token count as t < 0)
             int tpos0 = 0;
             if (conv_tile) tpos0 = ((wrow % p.L) + p.L) % p.L;
+            // no sequence start among the rows this warp's windows read: for
+            // the first quarter rows 1..31 (its rows 0..2 are not stored),
+            // for the others rows -3..31
+            const bool fast_rows = quarter == 0 ? (p.L >= 32 && tpos0 + 31 < p.L) : (tpos0 >= 3 && tpos0 + 31 < p.L);
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + b * kPAccCols;
             for (int c = 0; c < p.BN; c += cstep) {
                 const int col = ncol + c;
@@ -309,31 +338,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const int cc = col + 32 * hlf + lane;  // this lane's channel
                         const float4 wv = __ldg(reinterpret_cast<const float4 *>(p.conv_w) + min(cc, ncols - 1));
                         const float bj = __ldg(p.conv_b + min(cc, ncols - 1));
-                        const __half *xc = reinterpret_cast<const __half *>(X) + lane;  // column `lane`, row stride 34
-                        // window rows 32q-3 .. 32q-1, zero before the sequence start
+                        const __half *xc = reinterpret_cast<const __half *>(X) + lane;  // column `lane`
+                        uint32_t off[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) off[k] = ((((32 * hlf + lane) >> 3) ^ k) << 4) + ((lane & 7) << 1);
+                        const int r0 = quarter * 32;
+                        // window rows r0-3 .. r0-1, zero before the sequence start
                         float w0 = 0.f, w1 = 0.f, w2 = 0.f;
                         if (quarter > 0) {
-                            const int r0 = quarter * 32;
                             if (tpos0 >= 3) w0 = __half2float(xc[(r0 - 3) * (kPXPitch / 2)]);
                             if (tpos0 >= 2) w1 = __half2float(xc[(r0 - 2) * (kPXPitch / 2)]);
                             if (tpos0 >= 1) w2 = __half2float(xc[(r0 - 1) * (kPXPitch / 2)]);
                         }
-                        int t = tpos0;
-#pragma unroll 8
-                        for (int i = 0; i < 32; ++i) {
-                            const float x3 = __half2float(xc[(quarter * 32 + i) * (kPXPitch / 2)]);
-                            if (t == 0) w0 = w1 = w2 = 0.f;
-                            float acc = fmaf(w0, wv.x, 0.f);
-                            acc = fmaf(w1, wv.y, acc);
-                            acc = fmaf(w2, wv.z, acc);
-                            acc = fmaf(x3, wv.w, acc);
-                            acc += bj;
-                            const int sr = i - skip;
-                            if (sr >= 0) st_swizzled_h(box, sr, 32 * hlf + lane, silu_fast(acc));
-                            w0 = w1;
-                            w1 = w2;
-                            w2 = x3;
-                            t = (t + 1 == p.L) ? 0 : t + 1;
+                        if (quarter == 0) {
+                            if (fast_rows)
+                                conv_column<3, true>(xc, r0, w0, w1, w2, wv, bj, box, off, tpos0, p.L);
+                            else
+                                conv_column<3, false>(xc, r0, w0, w1, w2, wv, bj, box, off, tpos0, p.L);
+                        } else {
+                            if (fast_rows)
+                                conv_column<0, true>(xc, r0, w0, w1, w2, wv, bj, box, off, tpos0, p.L);
+                            else
+                                conv_column<0, false>(xc, r0, w0, w1, w2, wv, bj, box, off, tpos0, p.L);
                         }
                         ++nchunk;
                     }

@@ -257,8 +257,9 @@ def test_save_weights_round_trip(cuda):
 
 
 def test_fused_conv_forward_equals_unfused(cuda, monkeypatch):
-    """The forward with in_proj and the causal conv fused in one kernel gives
-    the same bits as the forward with them separate (MAMBA_CONV_FUSE=0)."""
+    """The forward with in_proj and the causal conv fused in one kernel
+    (MAMBA_CONV_FUSE=1) gives the same bits as the forward with them
+    separate (the default)."""
     rng = np.random.default_rng(110)
     cfg = mb.MambaConfig(128, 16, 4, 2, 2, mb.F16)
     layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
