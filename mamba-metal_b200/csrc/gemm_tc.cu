@@ -14,23 +14,25 @@
 // Structure: a persistent kernel run by CTA pairs (thread-block clusters of
 // two, cta_group::2).  A pair owns a 256 x BN output tile (BN <= 256): each
 // CTA loads 128 rows of A and BN/2 rows of W per 64-wide K block by TMA
-// (128-byte swizzle) into its own 5-stage ring, and one thread of the even
+// (128-byte swizzle) into its own 5-stage ring (4 with the conv), and one thread of the even
 // CTA issues tcgen05.mma with M = 256 that reads both CTAs' shared memory
 // and accumulates in both CTAs' TMEM (each CTA gets its 128 rows).  Per SM
 // and K block that is 32 KB of operands for a 128 x 256 x 64 slab, two
 // thirds of what one CTA alone would load for the same slab.  TMEM holds two
 // accumulators, so the epilogue of one tile overlaps the MMAs of the next.
 //
-// Roles (192 threads per CTA):
+// Roles (64 + 32 * epilogue warps threads per CTA):
 //   warp 0 lane 0  TMA producer.  Its copies complete on the even CTA's
 //                  stage barrier, which expects the bytes of both CTAs.
 //   warp 1         TMEM owner (both CTAs); in the even CTA one lane issues
 //                  the MMAs and commits them to both CTAs' barriers.
-//   warps 2-5      epilogue: TMEM -> registers -> a 128-byte-swizzled
-//                  shared-memory box of 32 rows per warp -> bulk tensor store
-//                  (or bulk tensor add for the residual), double-buffered
-//                  per warp; then the warp releases the accumulator to the
-//                  even CTA's MMA thread.
+//   warps 2..      epilogue (8 warps; 4 for the conv-fused variant): warp w
+//                  reads TMEM lane quarter w % 4, i.e. 32 rows, and a share
+//                  of the column chunks: TMEM -> registers -> a
+//                  128-byte-swizzled shared-memory box of 32 rows -> bulk
+//                  tensor store (or bulk tensor add for the residual),
+//                  double-buffered per warp; then the warp releases the
+//                  accumulator to the even CTA's MMA thread.
 // Every mbarrier wait is bounded (2 s); on timeout the role stops, bit 4 of
 // the device status is set, and both CTAs still reach the final cluster
 // barrier, so TMEM is freed and neither CTA exits while its peer may touch
@@ -55,18 +57,30 @@ namespace {
 
 constexpr int kPBK = 64;                          // K per stage: one 128-byte swizzle row
 constexpr int kPUK = 16;                          // K per MMA
-constexpr int kPStages = 5;
-constexpr int kPThreads = 192;
+// Plain epilogues: 8 epilogue warps (two per TMEM lane quarter, splitting
+// the tile's column chunks) and 5 stages.  The conv-fused epilogue: 4 warps
+// (its halo exchange pairs warps by quarter) and 4 stages, making room for
+// the conv input tile.
+template <bool CONV>
+struct ProjCfg {
+    static constexpr int kStages = CONV ? 4 : 5;
+    static constexpr int kEpiWarps = CONV ? 4 : 8;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+};
 constexpr int kPAccCols = 256;                    // TMEM columns per accumulator
 constexpr int kPTmemCols = 2 * kPAccCols;
 constexpr int kPStageA = 128 * kPBK * 2;          // 16 KB: this CTA's 128 rows of A
 constexpr int kPStageB = 128 * kPBK * 2;          // 16 KB: up to 128 rows of W
 constexpr int kPStage = kPStageA + kPStageB;
 constexpr int kPEpiBox = 32 * 128;                // 4 KB: 32 rows x 128 bytes
-constexpr int kPEpiBytes = 4 * 2 * kPEpiBox;      // 4 warps x 2 buffers
 constexpr int kPXPitch = 68;                      // bytes per row of the conv input tile (32 FP16 + pad)
 constexpr int kPXchBytes = 2 * 128 * kPXPitch;    // conv input tile [128 rows][32 cols] FP16, double-buffered
-constexpr int kPSmem = kPStages * kPStage + kPEpiBytes + kPXchBytes + 1024 /* alignment */ + 256 /* barriers */;
+template <bool CONV>
+constexpr int proj_smem_bytes() {
+    return ProjCfg<CONV>::kStages * kPStage + ProjCfg<CONV>::kEpiWarps * 2 * kPEpiBox + (CONV ? kPXchBytes : 0) +
+           1024 /* alignment */ + 256 /* barriers */;
+}
+static_assert(proj_smem_bytes<false>() <= 232448 && proj_smem_bytes<true>() <= 232448, "shared memory");
 constexpr unsigned kErrProjTimeout = 16u;
 
 struct ProjParams {
@@ -158,16 +172,19 @@ __device__ __forceinline__ void conv_column(const __half *__restrict__ xc, int r
 }
 
 template <bool CONV>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
     proj_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c_short,
                      const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_z_short,
                      const ProjParams p) {
+    constexpr int kPStages = ProjCfg<CONV>::kStages;
+    constexpr int kEpiWarps = ProjCfg<CONV>::kEpiWarps;
+    constexpr int kEpiBytes = kEpiWarps * 2 * kPEpiBox;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *epi = smem + kPStages * kPStage;
-    uint8_t *xch = epi + kPEpiBytes;  // conv input tiles
-    uint64_t *full = reinterpret_cast<uint64_t *>(epi + kPEpiBytes + kPXchBytes);
+    uint8_t *xch = epi + kEpiBytes;  // conv input tiles
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi + kEpiBytes + (CONV ? kPXchBytes : 0));
     uint64_t *empty = full + kPStages;
     uint64_t *tfull = empty + kPStages;
     uint64_t *tempty = tfull + 2;
@@ -189,7 +206,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA
+            mbar_init(&tempty[b], 2 * kEpiWarps);  // every epilogue warp of both CTAs
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -275,9 +292,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // before `halo` are not outputs: that warp stores a shorter box
         // (map *_short) from shared-memory row 0 = tile row `halo`.
         const int quarter = warp & 3;
+        const int egroup = (warp - 2) >> 2;  // column-chunk group: chunks egroup, egroup + groups, ...
+        constexpr int kGroups = kEpiWarps / 4;
         const int skip = quarter == 0 ? p.halo : 0;
         const int srow = lane - skip;  // this lane's row in the staged box (< 0: not stored)
-        uint8_t *boxes = epi + (warp - 2) * 2 * kPEpiBox;
+        uint8_t *boxes = epi + (warp - 2) * 2 * kPEpiBox;  // this warp's two staging boxes
         const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
         const bool f16 = p.mode == kProjF16;
         const int cstep = f16 ? 64 : 32;
@@ -309,7 +328,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // for the others rows -3..31
             const bool fast_rows = quarter == 0 ? (p.L >= 32 && tpos0 + 31 < p.L) : (tpos0 >= 3 && tpos0 + 31 < p.L);
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + b * kPAccCols;
-            for (int c = 0; c < p.BN; c += cstep) {
+            for (int c = egroup * cstep; c < p.BN; c += kGroups * cstep) {
                 const int col = ncol + c;
                 uint32_t v0[32];
                 uint32_t pk[32];  // FP16 output: 64 columns as 32 packed pairs
@@ -480,8 +499,8 @@ int device_info(DevInfo &out) {
     if ((int)cache.size() <= dev) cache.resize(dev + 1);
     DevInfo &d = cache[dev];
     if (!d.ready) {
-        MB_CUDA_TRY(
-            cudaFuncSetAttribute(proj_gemm_kernel<CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
+        MB_CUDA_TRY(cudaFuncSetAttribute(proj_gemm_kernel<CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         proj_smem_bytes<CONV>()));
         cudaLaunchConfig_t cfg{};
         cudaLaunchAttribute attr{};
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -489,8 +508,8 @@ int device_info(DevInfo &out) {
         attr.val.clusterDim.y = 1;
         attr.val.clusterDim.z = 1;
         cfg.gridDim = dim3(2 * 148, 1, 1);
-        cfg.blockDim = dim3(kPThreads, 1, 1);
-        cfg.dynamicSmemBytes = kPSmem;
+        cfg.blockDim = dim3(ProjCfg<CONV>::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = proj_smem_bytes<CONV>();
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
@@ -525,8 +544,8 @@ int launch_proj(const CUtensorMap *maps, const ProjParams &p, cudaStream_t st) {
     attr.val.clusterDim.y = 1;
     attr.val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kPThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPSmem;
+    cfg.blockDim = dim3(ProjCfg<CONV>::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = proj_smem_bytes<CONV>();
     cfg.stream = st;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
