@@ -492,7 +492,7 @@ def run_decode(args, world, rank, local):
 def run_scan(args, world, rank, local):
     import torch
     import mamba_b200 as mb
-    from mamba_b200.seqpar import sequence_parallel_scan
+    from mamba_b200.seqpar import NcclComm, sequence_parallel_scan_nccl
     Lg = args.seqlen or SCAN["seqlen"]
     if Lg % world:
         raise SystemExit("seqlen not divisible by ranks")
@@ -500,21 +500,32 @@ def run_scan(args, world, rank, local):
     torch.cuda.set_stream(stream)
     L = Lg // world
     D, N = SCAN["d_inner"], SCAN["d_state"]
+    # Every rank draws the whole sequence from one seed (for the parity check
+    # against a one-GPU scan) and scans its own time slice.
     g = torch.Generator(device="cuda")
-    g.manual_seed(77 + rank)
-    x = torch.randn((1, L, D), device="cuda", generator=g).half()
-    z = torch.randn((1, L, D), device="cuda", generator=g).half()
-    dr = (torch.randn((1, L, D), device="cuda", generator=g) * 0.5 - 4.6).float()
-    B = torch.randn((1, L, N), device="cuda", generator=g).half()
-    C = torch.randn((1, L, N), device="cuda", generator=g).half()
+    g.manual_seed(77)
+    xf = torch.randn((1, Lg, D), device="cuda", generator=g).half()
+    zf = torch.randn((1, Lg, D), device="cuda", generator=g).half()
+    drf = (torch.randn((1, Lg, D), device="cuda", generator=g) * 0.5 - 4.6).float()
+    Bf = torch.randn((1, Lg, N), device="cuda", generator=g).half()
+    Cf = torch.randn((1, Lg, N), device="cuda", generator=g).half()
+    s = slice(rank * L, (rank + 1) * L)
+    x, z, dr, B, C = (t[:, s].contiguous() for t in (xf, zf, drf, Bf, Cf))
     A = -torch.arange(1, N + 1, device="cuda", dtype=torch.float32).repeat(D, 1).contiguous()
     Dk = torch.ones(D, device="cuda")
+    comm = NcclComm() if world > 1 else None
+    y = torch.empty_like(x)
+    ws = None
 
     def step():
         if world == 1:
-            return mb.selective_scan(x, dr, A, B, C, D=Dk, z=z, return_final_state=True)
-        return sequence_parallel_scan(x, dr, A, B, C, D=Dk, z=z)
+            return mb.selective_scan(x, dr, A, B, C, D=Dk, z=z, return_final_state=True, y=y)
+        return sequence_parallel_scan_nccl(comm, x, dr, A, B, C, D=Dk, z=z, y=y, workspace=ws, stream=stream)
 
+    if world > 1:
+        need = mb.lib().mamba_selective_scan_seqpar_workspace(
+            ctypes_byref(mb._scan_args(x, dr, A, B, C, Dk, z, None, None, y, None, 0)), world)
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device="cuda")
     for _ in range(args.warmup):
         step()
     barrier(world)
@@ -523,12 +534,22 @@ def run_scan(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        _, h_last = step()
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier(world)
     t_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    # parity: this rank's slice (and, on the last rank, the final state)
+    # against the one-GPU scan of the whole sequence
+    yf, hf = mb.selective_scan(xf, drf, A, Bf, Cf, D=Dk, z=zf, return_final_state=True)
+    torch.cuda.synchronize()
+    ref = yf[:, s].float()
+    err_y = float((y.float() - ref).abs().max() / ref.abs().max())
+    err_h = float((h_last - hf).abs().max() / hf.abs().max()) if rank == world - 1 else 0.0
+    err = max_over_ranks(max(err_y, err_h), world)
+    if comm is not None:
+        comm.close()
     nbytes = Lg * D * (2 + 4 + 2 + 2) + Lg * N * 2 * 2 + D * N * 4 + D * 4
     value = nbytes * args.steps / (t_ms / 1e3) / 1e9
     peak, peak_src = peaks()
@@ -538,11 +559,24 @@ def run_scan(args, world, rank, local):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "x,B,C,z,y f16; delta f32; f32 state", "data": "synthetic",
                 "config": {"workload": "selective scan batch 1, d_inner 2048, d_state 16, L %d" % Lg,
-                           "parallelism": "sequence-sharded over %d ranks (all-gather of carries)" % world},
+                           "parallelism": ("sequence-sharded over %d ranks: mamba_selective_scan_seqpar "
+                                           "(ncclAllGather of the slice carries, %d NCCL ranks)" % (world, world))
+                           if world > 1 else "one GPU"},
                 "roofline": {"bound": "hbm", "achieved": value / world, "peak": peak, "unit": "GB/s",
                              "frac": value / world / peak, "peak_source": peak_src, "traffic": None},
+                "parity": {"normwise_rel_err": err, "tolerance": 2e-3, "pass": err < 2e-3,
+                           "checked": "each rank's slice of y and the last rank's final state against the "
+                                      "one-GPU scan of the whole sequence (max over ranks)"},
+                # chunked scan: summary + combine + output kernels; sharded:
+                # slice summary (2), compose (1), rescan (3), plus NCCL's
+                "gpu_launches": args.steps * (3 if world == 1 else 6),
                 "clocks": clk}
         print(json.dumps(line))
+
+
+def ctypes_byref(obj):
+    import ctypes
+    return ctypes.byref(obj)
 
 
 def run_mlp(args, world, rank, local):

@@ -284,6 +284,32 @@ int mamba_scan_summary(const MambaScanArgs *a, float *P, float *H, void *workspa
 int mamba_scan_compose_prefix(const float *PH, int world, int rank, int64_t count,
                               const float *h0, float *h_in, void *stream);
 
+/* Sequence-sharded mode as one call over NCCL: rank `rank` of `world`
+ * holds time slice `rank` of every sequence in `a` (x, delta, z, B, C, y of
+ * its slice; a->initial_state, if given, is the state entering slice 0 and
+ * must be the same on every rank).  On `stream` it computes its slice's
+ * summary, exchanges all summaries with one ncclAllGather of
+ * 2*batch*dim*dstate floats (the GPU-granularity carry exchange that
+ * prefix_scan.metal:19-40 does for tiles), composes the state entering its
+ * slice (mamba_scan_compose_prefix) and rescans the slice from it, writing
+ * y and a->final_state (on the last rank: the sequence's final state).
+ * nccl_comm is an ncclComm_t of exactly `world` ranks in which this process
+ * is `rank` (e.g. from mamba_nccl_comm_create).  Every rank must make the
+ * call (it contains a collective).  workspace: 256-byte aligned device
+ * memory of mamba_selective_scan_seqpar_workspace(a, world) bytes.  NCCL is
+ * loaded at run time (libnccl.so.2); without it the call fails with -1.
+ * 0 / -1. */
+size_t mamba_selective_scan_seqpar_workspace(const MambaScanArgs *a, int world);
+int mamba_selective_scan_seqpar(const MambaScanArgs *a, void *nccl_comm, int world, int rank, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
+/* NCCL communicator helpers for the call above: one rank creates a 128-byte
+ * id, the caller distributes it (any channel), and every rank creates its
+ * communicator on its current device.  0 / -1. */
+int mamba_nccl_unique_id(void *id128);
+int mamba_nccl_comm_create(const void *id128, int world, int rank, void **comm);
+int mamba_nccl_comm_destroy(void *comm);
+
 /* Depthwise causal conv (causal_conv1d.metal:21-45), width K, optional
  * bias and SiLU.  x, y strides {batch, time, channel}; w [dim, K] FP32;
  * bias [dim] FP32 or NULL.  x and y share `dtype`. */

@@ -66,7 +66,7 @@ def build(force=False, ptxas_verbose=False, jobs=None):
     logs = [l for _, l in results if l]
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < _newest(objs):
         cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + [
-            "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcublas", "-lcudart",
+            "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcublas", "-lcudart", "-ldl",
             "-Xlinker", "-rpath=" + os.path.join(CUDA_HOME, "lib64")]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

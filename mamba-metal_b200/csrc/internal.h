@@ -22,6 +22,14 @@ int bounded_wait_selftest(unsigned limit_us, cudaStream_t st);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st);
 
+// seqpar.cu
+size_t seqpar_workspace_bytes(const MambaScanArgs *a, int world);
+int seqpar_scan(const MambaScanArgs *a, void *comm, int world, int rank, void *ws, size_t ws_bytes,
+                cudaStream_t st);
+int nccl_unique_id(void *id);
+int nccl_comm_create(const void *id, int world, int rank, void **comm);
+int nccl_comm_destroy(void *comm);
+
 // conv.cu
 int causal_conv1d(const void *x, const int64_t *sx, const float *w, const float *bias, void *y,
                   const int64_t *sy, int batch, int L, int D, int K, int silu, int dtype,

@@ -1232,6 +1232,33 @@ int mamba_scan_compose_prefix(const float *PH, int world, int rank, int64_t coun
                                                                                                          : 0;
 }
 
+size_t mamba_selective_scan_seqpar_workspace(const MambaScanArgs *a, int world) {
+    return mb::seqpar_workspace_bytes(a, world);
+}
+
+int mamba_selective_scan_seqpar(const MambaScanArgs *a, void *nccl_comm, int world, int rank, void *workspace,
+                                size_t workspace_bytes, void *stream) {
+    mb::clear_error();
+    return mb::seqpar_scan(a, nccl_comm, world, rank, workspace, workspace_bytes, static_cast<cudaStream_t>(stream))
+               ? -1
+               : 0;
+}
+
+int mamba_nccl_unique_id(void *id128) {
+    mb::clear_error();
+    return mb::nccl_unique_id(id128) ? -1 : 0;
+}
+
+int mamba_nccl_comm_create(const void *id128, int world, int rank, void **comm) {
+    mb::clear_error();
+    return mb::nccl_comm_create(id128, world, rank, comm) ? -1 : 0;
+}
+
+int mamba_nccl_comm_destroy(void *comm) {
+    mb::clear_error();
+    return mb::nccl_comm_destroy(comm) ? -1 : 0;
+}
+
 int mamba_causal_conv1d(const void *x, const int64_t *x_stride, const float *w, const float *bias, void *y,
                         const int64_t *y_stride, int batch, int seqlen, int dim, int K, int silu, int dtype,
                         void *stream) {

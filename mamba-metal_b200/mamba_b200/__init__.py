@@ -99,6 +99,12 @@ _PROTOTYPES = {
     "mamba_selective_scan_noalloc": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p]),
     "mamba_scan_summary": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_void_p, c_void_p,
                                    c_size, c_void_p]),
+    "mamba_selective_scan_seqpar_workspace": (c_size, [ctypes.POINTER(MambaScanArgs), c_int]),
+    "mamba_selective_scan_seqpar": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_int, c_int, c_void_p, c_size,
+                                            c_void_p]),
+    "mamba_nccl_unique_id": (c_int, [c_void_p]),
+    "mamba_nccl_comm_create": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "mamba_nccl_comm_destroy": (c_int, [c_void_p]),
     "mamba_scan_compose_prefix": (c_int, [c_void_p, c_int, c_int, c_i64, c_void_p, c_void_p,
                                           c_void_p]),
     "mamba_causal_conv1d": (c_int, [c_void_p, ctypes.POINTER(c_i64), c_void_p, c_void_p, c_void_p,
