@@ -272,7 +272,9 @@ int mamba_selective_scan_noalloc(const MambaScanArgs *a, void *stream);
 /* Sequence-sharded mode, step 1: summary of this rank's slice of the
  * sequence: for every (b, d, n) the affine map h -> P*h + H that the slice
  * applies to its incoming state.  P, H: DEVICE FP32 [batch, dim, dstate].
- * y, z, C and the initial/final state in `a` are ignored. */
+ * y, z, C and the initial/final state in `a` are ignored.  workspace: at
+ * least mamba_scan_summary_workspace(a) bytes (0: may be NULL). */
+size_t mamba_scan_summary_workspace(const MambaScanArgs *a);
 int mamba_scan_summary(const MambaScanArgs *a, float *P, float *H, void *workspace,
                        size_t workspace_bytes, void *stream);
 

@@ -12,11 +12,15 @@ namespace mb {
 
 // scan.cu
 size_t scan_workspace_bytes(const MambaScanArgs *a);
+size_t chunked_workspace_bytes(const MambaScanArgs *a);
 int selective_scan(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream_t st);
 int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws_bytes,
                  cudaStream_t st);
 int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0,
                         float *h_in, cudaStream_t st);
+int scan_seqpar_pass1(const MambaScanArgs *a, float *P_tot, float *H_tot, void *ws, size_t ws_bytes,
+                      cudaStream_t st);
+int scan_seqpar_pass2(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream_t st);
 unsigned device_error_flags(bool clear);
 int bounded_wait_selftest(unsigned limit_us, cudaStream_t st);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();

@@ -1209,6 +1209,8 @@ int mamba_profile_read(MambaModel *m, int op, double *total_ms, int64_t *calls, 
 // ---- Part 3: kernels on device pointers --------------------------------------
 size_t mamba_selective_scan_workspace(const MambaScanArgs *a) { return mb::scan_workspace_bytes(a); }
 
+size_t mamba_scan_summary_workspace(const MambaScanArgs *a) { return mb::chunked_workspace_bytes(a); }
+
 int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes, void *stream) {
     mb::clear_error();
     return mb::selective_scan(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) ? -1 : 0;

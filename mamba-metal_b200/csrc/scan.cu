@@ -1007,6 +1007,16 @@ int launch_quad(const ScanKParams &kp, const MambaScanArgs *a, cudaStream_t st) 
 
 }  // namespace
 
+// Carry scratch of the time-chunked path for these args (whether or not a
+// single pass would be chosen instead).
+size_t chunked_workspace_bytes(const MambaScanArgs *a) {
+    if (!a || a->batch <= 0 || a->dim <= 0 || a->seqlen <= 0) return 0;
+    const int clen = choose_chunk_len(a->batch, a->seqlen, a->dim, a->chunk_len);
+    const int nc = ceil_div(a->seqlen, clen);
+    if (nc <= 1) return 0;
+    return 2 * sizeof(float) * (size_t)a->batch * nc * a->dim * a->dstate;
+}
+
 size_t scan_workspace_bytes(const MambaScanArgs *a) {
     if (!a || a->batch <= 0 || a->dim <= 0 || a->seqlen <= 0) return 0;
     if (use_quad(a)) return 0;
@@ -1062,7 +1072,7 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
         kp.sumH = H;
         return launch_scan_dtypes<kModeSummary>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st);
     }
-    const size_t need = scan_workspace_bytes(a);
+    const size_t need = chunked_workspace_bytes(a);
     MB_CHECK_ARG(ws != nullptr && ws_bytes >= need, "scan_summary: workspace too small");
     float *sumP = static_cast<float *>(ws);
     float *sumH = sumP + (size_t)a->batch * kp.nchunks * DN;
@@ -1070,6 +1080,53 @@ int scan_summary(const MambaScanArgs *a, float *P, float *H, void *ws, size_t ws
     kp.sumH = sumH;
     if (launch_scan_dtypes<kModeSummary>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st)) return -1;
     return launch_combine(sumP, sumH, nullptr, kp.nchunks, DN, a->batch, 0, P, H, st);
+}
+
+// Sequence-sharded mode in two passes over the slice (instead of a summary
+// pass followed by a full chunked scan, which would repeat the chunk
+// summaries).  Pass 1 leaves the chunk summaries in `ws` and writes the
+// slice's total map to P_tot / H_tot; pass 2 combines the stored summaries
+// from the entering state a->initial_state and runs the output pass.  Both
+// use the chunking choose_chunk_len gives these args, so `ws` (of
+// scan_workspace_bytes(a) bytes) carries the summaries between them.
+int scan_seqpar_pass1(const MambaScanArgs *a, float *P_tot, float *H_tot, void *ws, size_t ws_bytes,
+                      cudaStream_t st) {
+    if (validate(a)) return -1;
+    if (a->batch == 0 || a->dim == 0) return 0;
+    const int64_t DN = (int64_t)a->dim * a->dstate;
+    if (a->seqlen == 0) return launch_combine(nullptr, nullptr, nullptr, 0, DN, a->batch, 0, P_tot, H_tot, st);
+    const int clen = choose_chunk_len(a->batch, a->seqlen, a->dim, a->chunk_len);
+    ScanKParams kp = make_params(a, clen);
+    if (kp.nchunks == 1) {
+        kp.sumP = P_tot;
+        kp.sumH = H_tot;
+        return launch_scan_dtypes<kModeSummary>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st);
+    }
+    MB_CHECK_ARG(ws != nullptr && ws_bytes >= chunked_workspace_bytes(a), "scan_seqpar: workspace too small");
+    kp.sumP = static_cast<float *>(ws);
+    kp.sumH = kp.sumP + (size_t)a->batch * kp.nchunks * DN;
+    if (launch_scan_dtypes<kModeSummary>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st)) return -1;
+    return launch_combine(kp.sumP, kp.sumH, nullptr, kp.nchunks, DN, a->batch, 0, P_tot, H_tot, st);
+}
+
+int scan_seqpar_pass2(const MambaScanArgs *a, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (validate(a)) return -1;
+    if (a->batch == 0 || a->dim == 0) return 0;
+    if (a->seqlen == 0) return selective_scan(a, nullptr, 0, st);
+    MB_CHECK_ARG(a->y && a->C, "selective_scan: y and C are required");
+    const int clen = choose_chunk_len(a->batch, a->seqlen, a->dim, a->chunk_len);
+    ScanKParams kp = make_params(a, clen);
+    if (kp.nchunks == 1) {
+        kp.h_init = a->initial_state;
+        return launch_scan_dtypes<kModeOutput>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st);
+    }
+    MB_CHECK_ARG(ws != nullptr && ws_bytes >= chunked_workspace_bytes(a), "scan_seqpar: workspace too small");
+    const int64_t DN = (int64_t)a->dim * a->dstate;
+    float *sumP = static_cast<float *>(ws);
+    float *sumH = sumP + (size_t)a->batch * kp.nchunks * DN;
+    if (launch_combine(sumP, sumH, a->initial_state, kp.nchunks, DN, a->batch, 1, nullptr, nullptr, st)) return -1;
+    kp.h_init = sumH;
+    return launch_scan_dtypes<kModeOutput>(kp, a->x_dtype, a->delta_dtype, a->bc_dtype, st);
 }
 
 int scan_compose_prefix(const float *PH, int world, int rank, int64_t count, const float *h0, float *h_in,

@@ -6,10 +6,13 @@
 // Sources/CPURef/selective_scan_cpu.hpp:12-19, at GPU granularity as
 // Sources/Kernels/prefix_scan.metal:19-40 intended for tiles).  On the
 // caller's stream:
-//   1. summary of the local slice: (P, H) [batch, dim, dstate] FP32
+//   1. summary of the local slice: (P, H) [batch, dim, dstate] FP32 (when the
+//      slice is split into time chunks, their summaries are kept)
 //   2. ncclAllGather of the 2 * batch * dim * dstate floats (the only exchange)
 //   3. compose the summaries of ranks < r over the sequence's initial state
-//   4. rescan the local slice from that state, writing y and its final state
+//   4. the output pass over the local slice from that state (the kept chunk
+//      summaries combined from it), writing y and the slice's final state
+// so each slice is read twice, as in a one-GPU chunked scan.
 // NCCL is loaded at run time (libnccl.so.2, the copy the process already
 // has, e.g. PyTorch's), so the rest of the library works without it.
 #include <dlfcn.h>
@@ -84,7 +87,7 @@ size_t seqpar_workspace_bytes(const MambaScanArgs *a, int world) {
     if (!a || world < 1 || a->batch <= 0 || a->dim <= 0) return 0;
     const size_t count = (size_t)a->batch * a->dim * a->dstate;
     return align256(2 * count * 4) + align256((size_t)world * 2 * count * 4) + align256(count * 4) +
-           align256(scan_workspace_bytes(a));
+           align256(chunked_workspace_bytes(a));
 }
 
 int seqpar_scan(const MambaScanArgs *a, void *comm, int world, int rank, void *ws, size_t ws_bytes,
@@ -112,16 +115,17 @@ int seqpar_scan(const MambaScanArgs *a, void *comm, int world, int rank, void *w
     p += align256(count * 4);
     void *scan_ws = p;
     const size_t scan_ws_bytes = ws_bytes - (size_t)(p - static_cast<char *>(ws));
-    // 1. the slice's summary (independent of its entering state)
-    if (scan_summary(a, local, local + count, scan_ws, scan_ws_bytes, st)) return -1;
+    // 1. the slice's summary (independent of its entering state); its chunk
+    //    summaries stay in scan_ws for step 4
+    if (scan_seqpar_pass1(a, local, local + count, scan_ws, scan_ws_bytes, st)) return -1;
     // 2. every rank's summary
     MB_NCCL_TRY(nccl().all_gather(local, all, 2 * count, ncclFloat32, c, st), "ncclAllGather");
     // 3. the state entering this slice
     if (scan_compose_prefix(all, world, rank, (int64_t)count, a->initial_state, h_in, st)) return -1;
-    // 4. rescan from it
+    // 4. the output pass from it (chunk summaries combined, not recomputed)
     MambaScanArgs local_args = *a;
     local_args.initial_state = h_in;
-    return selective_scan(&local_args, scan_ws, scan_ws_bytes, st);
+    return scan_seqpar_pass2(&local_args, scan_ws, scan_ws_bytes, st);
 }
 
 int nccl_unique_id(void *id) {

@@ -95,6 +95,7 @@ _PROTOTYPES = {
     "mamba_profile_read": (c_int, [c_void_p, c_int, ctypes.POINTER(ctypes.c_double),
                                    ctypes.POINTER(c_i64), ctypes.POINTER(c_i64)]),
     "mamba_selective_scan_workspace": (c_size, [ctypes.POINTER(MambaScanArgs)]),
+    "mamba_scan_summary_workspace": (c_size, [ctypes.POINTER(MambaScanArgs)]),
     "mamba_selective_scan": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_size, c_void_p]),
     "mamba_selective_scan_noalloc": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p]),
     "mamba_scan_summary": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_void_p, c_void_p,
@@ -480,7 +481,7 @@ def scan_summary(x, delta, A, B, dt_bias=None, chunk_len=0, stream=None):
     P = torch.empty((bsz, dim, N), dtype=torch.float32, device=x.device)
     H = torch.empty_like(P)
     a = _scan_args(x, delta, A, B, None, None, None, dt_bias, None, None, None, chunk_len)
-    ws_bytes = lib().mamba_selective_scan_workspace(ctypes.byref(a))
+    ws_bytes = lib().mamba_scan_summary_workspace(ctypes.byref(a))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device) if ws_bytes else None
     _check(lib().mamba_scan_summary(ctypes.byref(a), _ptr(P), _ptr(H), _ptr(ws), ws_bytes,
                                     _stream(stream)), "mamba_scan_summary")

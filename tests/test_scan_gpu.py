@@ -293,3 +293,23 @@ def test_zero_length_and_empty_problems(cuda):
     torch.cuda.synchronize()
     assert y0.shape == (0, 5, D)
     assert mb.device_status() == 0
+
+
+def test_summary_on_a_four_lane_shape_sizes_its_own_workspace(cuda):
+    """Where the scan itself takes the four-lane single pass (no workspace),
+    the slice summary still splits time into chunks: its scratch comes from
+    mamba_scan_summary_workspace, and the summary's H (the map applied to a
+    zero state) equals the scan's final state from zero."""
+    import ctypes
+    bsz, L, D, N = 5, 1000, 1024, 16
+    x, dr, B, C, z, A, Dk = scan_inputs(41, bsz, L, D, N)
+    tx, tdr, tA = dev(r16(x), torch.float16), dev(r16(dr), torch.float16), dev(A)
+    tB, tC = dev(r16(B), torch.float16), dev(r16(C), torch.float16)
+    assert mb.scan_workspace_bytes(tx, tdr, tA, tB) == 0  # the scan runs four lanes per channel
+    a = mb._scan_args(tx, tdr, tA, tB, None, None, None, None, None, None, None, 0)
+    assert mb.lib().mamba_scan_summary_workspace(ctypes.byref(a)) > 0
+    P, H = mb.scan_summary(tx, tdr, tA, tB)
+    _, h = mb.selective_scan(tx, tdr, tA, tB, tC, D=dev(Dk), return_final_state=True)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    assert err(H, h.cpu().numpy()) < TOL32
