@@ -104,7 +104,8 @@ const char *mamba_last_error(void);
  * mamba_gated_mlp_up.  Bit 2: the same for mamba_linear (and the decode
  * projections that use it).  Bit 3: set by mamba_selftest_bounded_wait.
  * Bit 4: the same as bit 0 for the CTA-pair projection GEMM (the model's
- * forward projections, mamba_linear above 512 rows).
+ * forward projections, mamba_linear above 512 rows).  Bit 5: the same for
+ * the decode state update's bulk-copy waits (mamba_ssm_step, mamba_step).
  * Waits for the device; clear != 0 resets them. */
 unsigned mamba_device_status(int clear);
 

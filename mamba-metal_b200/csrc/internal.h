@@ -51,6 +51,7 @@ int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const f
              const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
              const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
              int xd, int dd, int bd, cudaStream_t st);
+unsigned step_error_flags(bool clear);
 
 // carries.cu
 int propagate_tile_carries(float *carries, int num_tiles, int64_t width, float *total, cudaStream_t st);

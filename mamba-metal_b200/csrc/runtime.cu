@@ -1080,7 +1080,9 @@ unsigned mamba_device_status(int clear) {
     const unsigned gemm = mb::gemm_error_flags(clear != 0);
     const unsigned lin = mb::linear_error_flags(clear != 0);
     const unsigned proj = mb::proj_error_flags(clear != 0);
-    return (scan == ~0u || gemm == ~0u || lin == ~0u || proj == ~0u) ? ~0u : (scan | gemm | lin | proj);
+    const unsigned step = mb::step_error_flags(clear != 0);
+    return (scan == ~0u || gemm == ~0u || lin == ~0u || proj == ~0u || step == ~0u) ? ~0u
+                                                                                       : (scan | gemm | lin | proj | step);
 }
 
 int mamba_selftest_bounded_wait(unsigned limit_us, void *stream) {

@@ -14,8 +14,11 @@
 
 #include "common.cuh"
 #include "scan_math.cuh"
+#include "tma.cuh"
 
 namespace mb {
+
+__device__ unsigned int g_step_error = 0;
 
 namespace {
 
@@ -203,6 +206,120 @@ __global__ void __launch_bounds__(128)
     }
 }
 
+// Bulk-copy variant of the kernel above for the common decode layout (FP16
+// activations, exactly 16 FP32 states per channel, 32-channel blocks
+// aligned): a CTA serves 32 channels x RB batch rows.  One thread issues RB
+// bulk copies of the CTA's 2 KB state run of each row into shared memory
+// (each completing on its own mbarrier), so RB x 2 KB per CTA and twelve
+// CTAs per SM are in flight at once instead of 16 B per thread; the rows
+// are updated in shared memory as they land (the same per-state operations
+// as above, so decode still equals the scan bit for bit) and go back with
+// bulk stores.  x, delta, z of all rows are loaded before the first wait.
+constexpr unsigned kErrStepTimeout = 32u;  // bit 5 of the device status
+
+template <int RB, typename Tx, typename Tdt, typename Tbc>
+__global__ void __launch_bounds__(128, 12)
+    ssm_step_bulk_kernel(const Tx *__restrict__ x, int64_t xrs, const Tdt *__restrict__ delta, int64_t drs,
+                         const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
+                         const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
+                         const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
+                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int batch, int D) {
+    constexpr int NS = 16, S = 4, kRowFloats = 32 * NS;  // one row's state run: 32 channels x 16 states
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *sst = reinterpret_cast<float *>(smem);  // [RB][32][16]
+    float *sBC = sst + RB * kRowFloats;            // [RB][2*NS]: B then C
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sBC + RB * 2 * NS);
+    const int tid = threadIdx.x, q = tid & 3, cl = tid >> 2;
+    const int d0 = blockIdx.x * 32, d = d0 + cl;
+    const int b0 = blockIdx.y * RB;
+    const int nr = min(RB, batch - b0);
+    if (tid == 0) {
+        for (int r = 0; r < RB; ++r) mbar_init(&bars[r], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int r = 0; r < nr; ++r) {
+            mbar_arrive_expect_tx(&bars[r], kRowFloats * 4);
+            bulk_load(sst + r * kRowFloats, state + ((int64_t)(b0 + r) * D + d0) * NS, kRowFloats * 4, &bars[r]);
+        }
+    }
+    for (int e = tid; e < nr * 2 * NS; e += 128) {
+        const int r = e / (2 * NS), j = e % (2 * NS);
+        const Tbc *src = j < NS ? Bm + (int64_t)(b0 + r) * bcrs + j : Cm + (int64_t)(b0 + r) * bcrs + (j - NS);
+        sBC[r * 2 * NS + j] = ld_f32(src);
+    }
+    const float4 a4 = *reinterpret_cast<const float4 *>(A + (int64_t)d * NS + q * S);
+    const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+    float ac[S], kI[S];
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+        ac[j] = av[j] * kLog2e;
+        kI[j] = fabsf(av[j]) > 1e-6f ? 1.0f / av[j] : 0.f;
+    }
+    const float bias = dt_bias ? dt_bias[d] : 0.f;
+    const float dsk = Dskip ? Dskip[d] : 0.f;
+    float xv[RB], draw[RB], zv[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+        const int b = b0 + (r < nr ? r : 0);
+        xv[r] = ld_f32(x + (int64_t)b * xrs + d);
+        draw[r] = ld_f32(delta + (int64_t)b * drs + d);
+        zv[r] = (z && q == 0) ? ld_f32(z + (int64_t)b * zrs + d) : 0.f;
+    }
+    __syncthreads();  // sBC
+    bool ok = true;
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+        if (r >= nr) break;
+        // warp-uniform verdict: the shuffles below need every lane
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[r], 0u))) {
+            ok = false;
+            break;
+        }
+        float *hp = sst + r * kRowFloats + cl * NS + q * S;
+        const float4 hv = *reinterpret_cast<const float4 *>(hp);
+        float h[S] = {hv.x, hv.y, hv.z, hv.w};
+        const float dt = softplus_fast(dt_bias ? __fadd_rn(draw[r], bias) : draw[r]);
+        const float *bc = sBC + r * 2 * NS;
+        float yp = 0.f;
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+            const int n = q * S + j;
+            const float a = ex2_approx(dt * ac[j]);
+            h[j] = state_update(a, xv[r] * bc[n], kI[j], dt, h[j]);
+            yp = fmaf(bc[NS + n], h[j], yp);
+        }
+        *reinterpret_cast<float4 *>(hp) = make_float4(h[0], h[1], h[2], h[3]);
+        yp += __shfl_xor_sync(0xffffffffu, yp, 1);
+        yp += __shfl_xor_sync(0xffffffffu, yp, 2);
+        if (q == 0) {
+            const float gate = z ? silu_fast(zv[r]) : 1.f;
+            y[(int64_t)(b0 + r) * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv[r], yp) * gate);
+        }
+    }
+    fence_proxy_async_smem();  // the updated rows are read by the bulk stores
+    const bool aborted = __syncthreads_or(!ok);
+    if (tid == 0) {
+        if (aborted) {
+            atomicOr(&g_step_error, kErrStepTimeout);
+            // copies still landing in this CTA's shared memory finish first
+            for (int r = 0; r < nr; ++r) mbar_wait_bounded(&bars[r], 0u);
+        } else {
+            for (int r = 0; r < nr; ++r)
+                bulk_store(state + ((int64_t)(b0 + r) * D + d0) * NS, sst + r * kRowFloats, kRowFloats * 4);
+            bulk_commit_group();
+            bulk_wait_group_read<0>();
+        }
+    }
+}
+
+// Rows per CTA and resident CTAs, measured on the 64-layer decode (batch 256,
+// 5120 channels): 4 rows with 12 CTAs per SM 43.5 us per layer; 8 rows / 8
+// CTAs 48.0; 4 / 16 48.6; 2 / 16 49.2; 16 rows 57.6; the four-lanes kernel
+// above 52.
+constexpr int kStepBulkRows = 4;
+
 template <int NS, typename Tx, typename Tdt, typename Tbc>
 int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
                 const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
@@ -216,6 +333,17 @@ int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, cons
 #define MAMBA_STEP_ROWS 4
 #endif
         constexpr int R = MAMBA_STEP_ROWS;
+        if (NS == 16 && N == 16 && aligned && D % 32 == 0 &&
+            (int64_t)(D / 32) * ceil_div(batch, kStepBulkRows) >= device_sm_count()) {
+            constexpr int RB = kStepBulkRows;
+            const int smem = RB * 32 * 16 * 4 + RB * 2 * 16 * 4 + RB * 8;
+            dim3 grid(D / 32, ceil_div(batch, RB));
+            ssm_step_bulk_kernel<RB, Tx, Tdt, Tbc><<<grid, 128, smem, st>>>(
+                static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
+                static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
+                static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, batch, D);
+            return launch_status("ssm_step (bulk copies) kernel");
+        }
         const bool many = (int64_t)ceil_div(D, 32) * ceil_div(batch, R) >= 2LL * device_sm_count();
         if (many) {
             dim3 grid(ceil_div(D, 32), ceil_div(batch, R));
@@ -280,6 +408,16 @@ int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const f
                                                     zrs, y, yrs, state, batch, D, N, st);
     set_error("ssm_step: unsupported dtype combination");
     return -1;
+}
+
+unsigned step_error_flags(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_step_error, sizeof(v)) != cudaSuccess) return ~0u;
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_step_error, &z, sizeof(z));
+    }
+    return v;
 }
 
 }  // namespace mb

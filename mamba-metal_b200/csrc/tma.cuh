@@ -161,6 +161,26 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
         : "memory");
 }
 
+// ---- untiled bulk copies ------------------------------------------------------
+// `bytes` contiguous bytes global -> this CTA's shared memory, completing on
+// `bar` by transaction bytes (both addresses 16-byte aligned, bytes a
+// multiple of 16).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// `bytes` contiguous bytes this CTA's shared memory -> global, tracked by
+// the bulk-group mechanism below.
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+
 // ---- bulk tensor stores (shared -> global) ---------------------------------
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) reads of them.

@@ -204,3 +204,32 @@ def test_ssm_step_multirow_kernel(cuda, misalign):
         torch.cuda.synchronize()
         assert err(y, yr) < TOL16
     assert err(st, st_ref) < TOL32
+
+
+def test_ssm_step_bulk_copy_kernel(cuda):
+    """Enough 32-channel x 16-row blocks to take the bulk-copy FP16 decode
+    kernel (3072 channels x batch 40: the last row block holds 8 rows): the
+    outputs match the oracle step, and T steps leave exactly the scan's final
+    state (the per-state operations are the scan's)."""
+    bsz, L, D, N = 40, 6, 3072, 16
+    x, dr, B, C, z, A, Dk = scan_inputs(23, bsz, L, D, N)
+    x, dr, B, C, z = map(r16, (x, dr, B, C, z))
+    bias = np.random.default_rng(2).normal(0, 0.5, D).astype(np.float32)
+    st_ref = np.zeros((bsz, D, N), np.float32)
+    st = torch.zeros((bsz, D, N), device="cuda")
+    tA, tD, tb = dev(A), dev(Dk), dev(bias)
+    tx, tdr, tB, tC, tz = (dev(a, torch.float16) for a in (x, dr, B, C, z))
+    ys = []
+    for t in range(L):
+        yr = oracle.ssm_step(x[:, t], dr[:, t], B[:, t], C[:, t], A, Dk, st_ref, z=z[:, t], dt_bias=bias)
+        y = mb.ssm_step(tx[:, t], tdr[:, t], tA, tB[:, t], tC[:, t], st, D=tD, z=tz[:, t], dt_bias=tb)
+        torch.cuda.synchronize()
+        assert err(y, yr) < TOL16
+        ys.append(y)
+    assert mb.device_status() == 0
+    assert err(st, st_ref) < TOL32
+    y_scan, h_scan = mb.selective_scan(tx, tdr, tA, tB, tC, D=tD, z=tz, dt_bias=tb, return_final_state=True)
+    torch.cuda.synchronize()
+    assert torch.equal(st, h_scan)
+    # y sums C*h in another order (four lanes' partial sums), so not bitwise
+    assert err(torch.stack(ys, 1), y_scan.float().cpu().numpy()) < TOL16
