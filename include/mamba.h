@@ -241,6 +241,21 @@ size_t mamba_selective_scan_workspace(const MambaScanArgs *a);
 int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes,
                          void *stream);
 
+/* The fused selective scan with the layer's dt_proj computed inside it
+ * (linear_f16 of projection.metal:32-49 for dt_proj, MambaRuntime.cpp:98,
+ * folded into selective_scan.metal:84-244): delta = dt_r @ w_dt^T with FP32
+ * accumulation on the tensor cores, rounded to FP16 (the value a separate
+ * FP16 GEMM would store), then dt = softplus(delta + dt_bias) as in
+ * mamba_selective_scan; a->delta is ignored.  dt_r FP16 [batch, seqlen,
+ * dt_rank] with element strides dt_r_stride = {batch, time} (channel stride
+ * 1; e.g. the first dt_rank columns of x_proj's output); w_dt FP16
+ * [dim, dt_rank] (dt_proj transposed, K-major).  Requires FP16 x, z, B, C,
+ * 16 states, dt_rank a multiple of 8 up to 128, channel-contiguous 16-byte
+ * aligned rows, batch * ceil(dim / 128) >= the GPU's SM count (one pass
+ * over time, no workspace), a compute capability 10.x GPU.  0 / -1. */
+int mamba_selective_scan_dtproj(const MambaScanArgs *a, const void *dt_r, const int64_t *dt_r_stride, const void *w_dt,
+                                int dt_rank, void *stream);
+
 /* The fused selective scan without a caller workspace: it allocates no
  * device memory (no cudaMalloc, cudaFree or allocating library call).  No
  * counterpart in the reference.  For callers that cannot allocate device

@@ -25,6 +25,9 @@ unsigned device_error_flags(bool clear);
 int bounded_wait_selftest(unsigned limit_us, cudaStream_t st);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 int selective_scan_noalloc(const MambaScanArgs *a, cudaStream_t st);
+bool scan_dtproj_supported(const MambaScanArgs *a, int R);
+int selective_scan_dtproj(const MambaScanArgs *a, const void *dt_r, const int64_t *dr_stride, const void *w_dt,
+                          int R, cudaStream_t st);
 
 // seqpar.cu
 size_t seqpar_workspace_bytes(const MambaScanArgs *a, int world);

@@ -258,6 +258,7 @@ struct Model {
         if (const char *h = std::getenv("MAMBA_HOST_CHUNKS")) host_chunks = std::max(0, std::atoi(h));
         if (const char *pj = std::getenv("MAMBA_PROJ")) proj_tc = std::atoi(pj) != 0;
         if (const char *cf = std::getenv("MAMBA_CONV_FUSE")) conv_fuse = std::atoi(cf) != 0;
+        if (const char *df = std::getenv("MAMBA_DT_FUSE")) dt_fuse = std::atoi(df) != 0;
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -333,6 +334,15 @@ struct Model {
     bool conv_fuse = false;
     bool fuse_conv(int64_t T, int L) const {
         return conv_fuse && proj_tc && act == MAMBA_F16 && T > kTcRows && proj_conv_supported(T, L, D, M, K);
+    }
+
+    // dt_proj folded into the scan (selective_scan_dtproj) wherever that
+    // kernel applies: FP16, 16 states, dt_rank a multiple of 8 up to 128,
+    // x_proj rows 16-byte aligned, one 128-channel CTA per SM or more.
+    // MAMBA_DT_FUSE=0 keeps the separate GEMM.
+    bool dt_fuse = true;
+    bool fuse_dt(const MambaScanArgs &sa) const {
+        return dt_fuse && act == MAMBA_F16 && (XD * 2) % 16 == 0 && scan_dtproj_supported(&sa, R);
     }
 
     bool use_proj(int64_t rows, int k, int lda, int ldc, int c_dtype) const {
@@ -496,14 +506,20 @@ struct Model {
                     return -1;
                 o.kernels = last_gemm_kernels;
             }
-            {
+            MambaScanArgs sa = scan_args(w, ar, batch, L);
+            const bool fdt = fuse_dt(sa);
+            if (!fdt) {
                 OpScope o(prof, MAMBA_OP_DT_PROJ, st, 0);
                 if (gemm(st, T, D, R, ar.xdbc, XD, w.w_dt_t, ar.draw, D, act, 0.f, ar.lin_ws, ar.lin_ws_bytes))
                     return -1;
                 o.kernels = last_gemm_kernels;
             }
-            {
-                MambaScanArgs sa = scan_args(w, ar, batch, L);
+            if (fdt) {
+                // dt_proj inside the scan (tcgen05 from TMEM-resident W_dt)
+                OpScope o(prof, MAMBA_OP_SCAN, st, 1);
+                const int64_t dr_stride[2] = {(int64_t)L * XD, XD};
+                if (selective_scan_dtproj(&sa, ar.xdbc, dr_stride, w.w_dt_t, R, st)) return -1;
+            } else {
                 OpScope o(prof, MAMBA_OP_SCAN, st, ar.scan_ws_bytes ? 3 : 1);
                 if (selective_scan(&sa, ar.scan_ws, ar.scan_ws_bytes, st)) return -1;
             }
@@ -1216,6 +1232,12 @@ size_t mamba_scan_summary_workspace(const MambaScanArgs *a) { return mb::chunked
 int mamba_selective_scan(const MambaScanArgs *a, void *workspace, size_t workspace_bytes, void *stream) {
     mb::clear_error();
     return mb::selective_scan(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) ? -1 : 0;
+}
+
+int mamba_selective_scan_dtproj(const MambaScanArgs *a, const void *dt_r, const int64_t *dt_r_stride, const void *w_dt,
+                                int dt_rank, void *stream) {
+    mb::clear_error();
+    return mb::selective_scan_dtproj(a, dt_r, dt_r_stride, w_dt, dt_rank, static_cast<cudaStream_t>(stream)) ? -1 : 0;
 }
 
 int mamba_selective_scan_noalloc(const MambaScanArgs *a, void *stream) {

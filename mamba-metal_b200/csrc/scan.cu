@@ -41,8 +41,10 @@
 #include <vector>
 
 #include "common.cuh"
+#include "internal.h"
 #include "scan_math.cuh"
 #include "tma.cuh"
+#include "umma.cuh"
 
 namespace mb {
 
@@ -464,6 +466,227 @@ __global__ void __launch_bounds__(CH, kTmaMinCtas)
         return;
     }
     if (dvalid) write_epilogue<NS>(p, SUMMARY, b, chunk, d, t_end, h, P);
+}
+
+// ---- the scan with dt_proj on the tensor cores --------------------------------
+// The layer's dt_proj (draw = dt_r @ W_dt^T, K = dt_rank <= 128) folded into
+// the one-thread TMA scan, so the [T, d_inner] draw tensor is never written
+// to or read from HBM.  Per CTA (128 channels): W_dt's 128 rows live in TMEM
+// (lane = channel, K along columns, two FP16 per column), loaded once.  Per
+// 16-step tile the TMA ring brings the dt_r tile [16 x dt_rank] (FP16,
+// 128-byte swizzle) in place of the delta tile; one thread issues
+// tcgen05.mma (M 128 channels, N 16 steps, A from TMEM, B from shared
+// memory) into one of three 16-column TMEM accumulators, a tile ahead of
+// its use, and each thread reads its channel's 16 values with tcgen05.ld,
+// rounds them to FP16 (the values the separate GEMM would store) and writes
+// them over the consumed dt_r tile, where the unchanged recurrence reads
+// them as its delta tile.  Every wait is bounded; TMEM is freed on every
+// path.
+template <int ST>
+struct DtLayout {
+    static constexpr int kXB = kTmaTT * kScanCH * 2;  // x or z tile, FP16
+    static constexpr int kDB = 2 * kTmaTT * 128;      // dt_r: two [16 x 64] FP16 boxes; later the FP16 draw tile
+    static constexpr int kBCB = kTmaTT * 16 * 2;      // B or C tile, FP16
+    static constexpr int kOffD = kXB, kOffZ = kXB + kDB, kOffB = 2 * kXB + kDB, kOffC = kOffB + kBCB;
+    static constexpr int kStage = (kOffC + kBCB + 1023) / 1024 * 1024;  // swizzled boxes need 1 KB alignment
+    static constexpr int kBC = 2 * kTmaTT * 2 * 16 * 4;                // double-buffered FP32 B/C
+    static constexpr int kBytes = 1024 + ST * kStage + kBC + (2 * ST + 1) * 8 + 16;
+    static_assert(kDB == kTmaTT * kScanCH * 2, "the draw tile reuses the dt_r slot");
+};
+constexpr int kDtMaxRank = 128;
+constexpr int kDtTmemCols = 128;  // W_dt (64 columns) + three 16-column accumulators
+
+template <int ST>
+__global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
+    scan_dtmma_kernel(const ScanKParams p, const __grid_constant__ CUtensorMap tmx,
+                      const __grid_constant__ CUtensorMap tmdr, const __grid_constant__ CUtensorMap tmz,
+                      const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+                      const __half *__restrict__ wdt, int R) {
+    constexpr int NS = 16, CH = kScanCH, TT = kTmaTT;
+    using Lay = DtLayout<ST>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);                  // [2][TT][2*NS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ST * Lay::kStage + Lay::kBC);  // [ST] copies landed
+    uint64_t *mbars = bars + ST;                                                       // [ST] draw tile in TMEM
+    uint64_t *drain = mbars + ST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int b = blockIdx.z;
+    const int d0 = blockIdx.x * CH, d = d0 + tid;
+    const bool dvalid = d < p.D;
+    const int N = p.N, L = p.L;
+    const int ntiles = (L + TT - 1) / TT;
+    const bool has_z = p.z != nullptr;
+    const int nkb = (R + 63) / 64;  // 64-wide K boxes of dt_r (zero past dt_rank)
+    const uint32_t tx_bytes = Lay::kXB + nkb * TT * 128 + (has_z ? Lay::kXB : 0) + 2u * (uint32_t)(N * TT * 2);
+    const uint32_t idesc = idesc_f16_f32acc(128, TT);
+
+    float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
+    const bool small = load_channel_consts<NS, false>(p.A, d, N, dvalid, Ac, kI);
+    if (dvalid) load_initial_state<NS>(p, b, 0, d, h, P);
+    else load_initial_state<NS>(ScanKParams{}, 0, 0, 0, h, P);
+    const bool has_bias = p.dt_bias != nullptr;
+    const float bias = (has_bias && dvalid) ? p.dt_bias[d] : 0.f;
+    const float dskip = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
+
+    if (tid == 0) {
+        prefetch_tensormap(&tmx);
+        prefetch_tensormap(&tmdr);
+        if (has_z) prefetch_tensormap(&tmz);
+        prefetch_tensormap(&tmB);
+        prefetch_tensormap(&tmC);
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&bars[s], 1);
+            mbar_init(&mbars[s], 1);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, kDtTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    const bool any_small = __syncthreads_or(small);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // this channel's row of W_dt (K-major, zero past dt_rank) as 64 columns of
+    // packed FP16 pairs, 16 columns at a time
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(wdt + (int64_t)(dvalid ? d : 0) * R);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t wr[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int g = 4 * c4 + i;  // 8 FP16 per 16-byte load
+                const uint4 v = (dvalid && 8 * g < R) ? src[g] : make_uint4(0u, 0u, 0u, 0u);
+                wr[4 * i] = v.x;
+                wr[4 * i + 1] = v.y;
+                wr[4 * i + 2] = v.z;
+                wr[4 * i + 3] = v.w;
+            }
+            tmem_st_32x32b_x16(tmem + lane_base + 16 * c4, wr);
+        }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    auto issue = [&](int tile, int s) {
+        uint8_t *stg = smem + s * Lay::kStage;
+        const int t = tile * TT;
+        mbar_arrive_expect_tx(&bars[s], tx_bytes);
+        tma_load_3d(stg, &tmx, &bars[s], d0, t, b);
+        for (int kb = 0; kb < nkb; ++kb) tma_load_3d(stg + Lay::kOffD + kb * TT * 128, &tmdr, &bars[s], kb * 64, t, b);
+        if (has_z) tma_load_3d(stg + Lay::kOffZ, &tmz, &bars[s], d0, t, b);
+        tma_load_3d(stg + Lay::kOffB, &tmB, &bars[s], 0, t, b);
+        tma_load_3d(stg + Lay::kOffC, &tmC, &bars[s], 0, t, b);
+    };
+    // One thread: the draw tile of `tile` (stage s) into accumulator s.
+    auto issue_mma = [&](int s) {
+        tc_fence_after();
+        const uint32_t b_addr = smem_u32(smem + s * Lay::kStage + Lay::kOffD);
+        const uint32_t d_tmem = tmem + 64 + 16 * s;
+        for (int kk = 0; kk < 4 * nkb; ++kk)
+            umma_f16_ts(d_tmem, tmem + 8 * kk, smem_desc_sw128(b_addr + (kk >> 2) * TT * 128 + (kk & 3) * 32), idesc,
+                        kk != 0);
+        umma_commit(&mbars[s]);
+    };
+    auto stage_bc = [&](int s, int t0, float *dst) {
+        const uint8_t *stg = smem + s * Lay::kStage;
+        convert_bc<NS, CH, TT, __half, false>(reinterpret_cast<const __half *>(stg + Lay::kOffB),
+                                              reinterpret_cast<const __half *>(stg + Lay::kOffC), dst, N, t0, L);
+    };
+    if (tid == 0)
+        for (int s = 0; s < min(ST, ntiles); ++s) issue(s, s);
+
+    bool ok0 = true;
+    if (ntiles > 0) {
+        ok0 = mbar_wait_bounded(&bars[0], 0u);
+        if (ok0) {
+            if (tid == 0) issue_mma(0);
+            stage_bc(0, 0, bcf);
+        }
+    }
+    int i = 0;
+    bool aborted = __syncthreads_or(!ok0);
+    for (; !aborted && i < ntiles; ++i) {
+        const int s = i % ST;
+        const int t0 = i * TT;
+        const int nt = min(TT, L - t0);
+        const uint32_t ph = (uint32_t)((i / ST) & 1);
+        bool ok = true;
+        // the next tile's draw is computed while this one is scanned
+        if (tid == 0 && i + 1 < ntiles) {
+            const int s1 = (i + 1) % ST;
+            if (mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1)))
+                issue_mma(s1);
+            else
+                ok = false;
+        }
+        ok = ok && mbar_wait_bounded(&bars[s], ph) && mbar_wait_bounded(&mbars[s], ph);
+        ok = __all_sync(0xffffffffu, ok);  // the TMEM load below is warp-collective
+        uint8_t *stg = smem + s * Lay::kStage;
+        if (ok) {
+            tc_fence_after();
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(tmem + lane_base + 64 + 16 * s, v);
+            tmem_wait_ld();
+            // over the consumed dt_r boxes: this thread's column of the FP16 draw tile
+            __half *sD = reinterpret_cast<__half *>(stg + Lay::kOffD);
+#pragma unroll
+            for (int tt = 0; tt < TT; ++tt) sD[tt * CH + tid] = __float2half_rn(__uint_as_float(v[tt]));
+            if (dvalid) {
+                const __half *sX = reinterpret_cast<const __half *>(stg);
+                const __half *sZ = reinterpret_cast<const __half *>(stg + Lay::kOffZ);
+                const float *sBC = bcf + (i & 1) * TT * 2 * NS;
+                if (any_small)
+                    run_steps<NS, CH, kSubTT, TT, false, false, true>(p, nt, t0, b, d, sX, sD, sZ, sBC, has_bias,
+                                                                     bias, dskip, has_z, h, Ac, kI, P);
+                else
+                    run_steps<NS, CH, kSubTT, TT, false, false, false>(p, nt, t0, b, d, sX, sD, sZ, sBC, has_bias,
+                                                                      bias, dskip, has_z, h, Ac, kI, P);
+            }
+        }
+        if (i + 1 < ntiles) {
+            float *next = bcf + ((i + 1) & 1) * TT * 2 * NS;
+            const int s1 = (i + 1) % ST;
+            const bool ok1 = mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1));
+            if (ok1) stage_bc(s1, t0 + TT, next);
+            ok = ok && ok1;
+        }
+        // the stage's shared memory is overwritten by the next copies
+        fence_proxy_async_smem();
+        tc_fence_before();
+        if (__syncthreads_or(!ok)) {
+            aborted = true;
+            break;
+        }
+        tc_fence_after();
+        if (tid == 0 && i + ST < ntiles) issue(i + ST, s);
+    }
+    if (tid == 0) {
+        // every issued MMA has finished before TMEM is freed
+        umma_commit(drain);
+        if (!mbar_wait_bounded(drain, 0u)) aborted = true;
+        if (aborted) {
+            atomicOr(&g_device_error, kErrTmaTimeout);
+            for (int j = i; j < min(i + ST, ntiles); ++j)
+                mbar_wait_bounded(&bars[j % ST], (uint32_t)((j / ST) & 1));
+        }
+    }
+    tc_fence_before();
+    aborted = __syncthreads_or(aborted);
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kDtTmemCols);
+    }
+    if (!aborted && dvalid) write_epilogue<NS>(p, false, b, 0, d, L, h, P);
 }
 
 // ---- four lanes per channel (few channels, single pass) ----------------------
@@ -1006,6 +1229,75 @@ int launch_quad(const ScanKParams &kp, const MambaScanArgs *a, cudaStream_t st) 
 }
 
 }  // namespace
+
+namespace {
+
+// 3-D map of dt_r (the first dt_rank columns of x_proj's output): dims
+// {dt_rank, L, batch}, box [64 x 16 steps], 128-byte swizzle (the K-major
+// B-operand layout of tcgen05.mma); columns past dt_rank read zeros.
+bool encode_dt_r(CUtensorMap *m, const void *ptr, int R, int L, int B, const int64_t *st) {
+    auto fn = tensor_map_encoder();
+    if (!fn || !ptr || reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    const int64_t row = st[1] * 2;
+    int64_t bat = st[0] * 2;
+    if (row <= 0 || row % 16 || row < (int64_t)R * 2) return false;
+    if (B == 1) bat = row * std::max(L, 1);
+    if (bat <= 0 || bat % 16) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)R, (cuuint64_t)L, (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)row, (cuuint64_t)bat};
+    cuuint32_t box[3] = {64, (cuuint32_t)kTmaTT, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool scan_dtproj_supported(const MambaScanArgs *a, int R) {
+    if (!a || a->batch <= 0 || a->dim <= 0 || a->seqlen <= 0) return false;
+    if (a->x_dtype != MAMBA_F16 || a->bc_dtype != MAMBA_F16 || a->dstate != 16 || a->chunk_len > 0) return false;
+    if (R < 8 || R > kDtMaxRank || R % 8) return false;
+    return (int64_t)a->batch * ceil_div(a->dim, kScanCH) >= device_sm_count();
+}
+
+int selective_scan_dtproj(const MambaScanArgs *a, const void *dt_r, const int64_t *dr_stride, const void *w_dt,
+                          int R, cudaStream_t st) {
+    if (validate(a)) return -1;
+    if (a->batch == 0 || a->dim == 0 || a->seqlen == 0) return selective_scan(a, nullptr, 0, st);
+    MB_CHECK_ARG(dt_r && w_dt && dr_stride && a->y && a->C, "selective_scan_dtproj: null pointer");
+    MB_CHECK_ARG(a->x_dtype == MAMBA_F16 && a->bc_dtype == MAMBA_F16 && a->dstate == 16,
+                 "selective_scan_dtproj: needs FP16 x, z, B, C and 16 states");
+    MB_CHECK_ARG(R >= 8 && R <= kDtMaxRank && R % 8 == 0,
+                 "selective_scan_dtproj: dt_rank must be a multiple of 8 in 8..128");
+    MB_CHECK_ARG(reinterpret_cast<uintptr_t>(w_dt) % 16 == 0, "selective_scan_dtproj: w_dt must be 16-byte aligned");
+    MB_CHECK_ARG(a->chunk_len == 0 && scan_dtproj_supported(a, R),
+                 "selective_scan_dtproj: needs batch * ceil(dim / 128) >= the SM count (one pass over time)");
+    int dev = 0, major = 0;
+    MB_CUDA_TRY(cudaGetDevice(&dev));
+    MB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MB_CHECK_ARG(major == 10, "selective_scan_dtproj: needs a compute capability 10.x GPU (tcgen05)");
+    ScanKParams kp = make_params(a, a->seqlen);
+    kp.h_init = a->initial_state;
+    CUtensorMap maps[5];  // x, dt_r, z, B, C
+    const bool ok = encode_map(&maps[0], kp.x, MAMBA_F16, kp.D, kp.L, kp.batch, kp.sx, kScanCH) &&
+                    encode_dt_r(&maps[1], dt_r, R, kp.L, kp.batch, dr_stride) &&
+                    (!kp.z || encode_map(&maps[2], kp.z, MAMBA_F16, kp.D, kp.L, kp.batch, kp.sz, kScanCH)) &&
+                    encode_map(&maps[3], kp.B, MAMBA_F16, kp.N, kp.L, kp.batch, kp.sB, kp.N) &&
+                    encode_map(&maps[4], kp.C, MAMBA_F16, kp.N, kp.L, kp.batch, kp.sC, kp.N);
+    MB_CHECK_ARG(ok, "selective_scan_dtproj: a tensor does not meet the TMA layout rules "
+                     "(channel-contiguous 16-byte aligned rows)");
+    if (!kp.z) maps[2] = maps[0];  // unused by the kernel
+    constexpr int ST = kTmaStages;
+    auto kern = scan_dtmma_kernel<ST>;
+    const int smem = DtLayout<ST>::kBytes;
+    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    dim3 grid(ceil_div(kp.D, kScanCH), 1, kp.batch);
+    kern<<<grid, kScanCH, smem, st>>>(kp, maps[0], maps[1], maps[2], maps[3], maps[4],
+                                      static_cast<const __half *>(w_dt), R);
+    return launch_status("selective scan with dt_proj (tcgen05) kernel");
+}
 
 // Carry scratch of the time-chunked path for these args (whether or not a
 // single pass would be chosen instead).

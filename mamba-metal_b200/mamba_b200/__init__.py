@@ -98,6 +98,8 @@ _PROTOTYPES = {
     "mamba_scan_summary_workspace": (c_size, [ctypes.POINTER(MambaScanArgs)]),
     "mamba_selective_scan": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_size, c_void_p]),
     "mamba_selective_scan_noalloc": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p]),
+    "mamba_selective_scan_dtproj": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, ctypes.POINTER(c_i64), c_void_p,
+                                            c_int, c_void_p]),
     "mamba_scan_summary": (c_int, [ctypes.POINTER(MambaScanArgs), c_void_p, c_void_p, c_void_p,
                                    c_size, c_void_p]),
     "mamba_selective_scan_seqpar_workspace": (c_size, [ctypes.POINTER(MambaScanArgs), c_int]),
@@ -465,6 +467,27 @@ def selective_scan(x, delta, A, B, C, D=None, z=None, dt_bias=None, initial_stat
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device) if ws_bytes else None
     _check(lib().mamba_selective_scan(ctypes.byref(a), _ptr(ws), ws_bytes, _stream(stream)),
            "mamba_selective_scan")
+    return (y, hN) if return_final_state else y
+
+
+def selective_scan_dtproj(x, dt_r, w_dt, A, B, C, D=None, z=None, dt_bias=None, initial_state=None,
+                          return_final_state=False, y=None, stream=None):
+    """Selective scan with delta = dt_r @ w_dt^T computed inside
+    (mamba_selective_scan_dtproj).  x, z: FP16 [batch, L, dim]; dt_r: FP16
+    [batch, L, dt_rank] view with channel stride 1; w_dt: FP16 [dim, dt_rank]
+    contiguous; B, C FP16 [batch, L, 16]."""
+    torch = _torch()
+    bsz, L, dim = x.shape
+    N = A.shape[1]
+    assert dt_r.stride(2) == 1 and w_dt.is_contiguous() and w_dt.shape[0] == dim
+    if y is None:
+        y = torch.empty((bsz, L, dim), dtype=x.dtype, device=x.device)
+    hN = torch.empty((bsz, dim, N), dtype=torch.float32, device=x.device) if return_final_state else None
+    a = _scan_args(x, x, A, B, C, D, z, dt_bias, initial_state, y, hN, 0)
+    a.delta_dtype = F16
+    st = (c_i64 * 2)(dt_r.stride(0), dt_r.stride(1))
+    _check(lib().mamba_selective_scan_dtproj(ctypes.byref(a), _ptr(dt_r), st, _ptr(w_dt), w_dt.shape[1],
+                                             _stream(stream)), "mamba_selective_scan_dtproj")
     return (y, hN) if return_final_state else y
 
 
