@@ -336,11 +336,14 @@ struct Model {
         return conv_fuse && proj_tc && act == MAMBA_F16 && T > kTcRows && proj_conv_supported(T, L, D, M, K);
     }
 
-    // dt_proj folded into the scan (selective_scan_dtproj) wherever that
-    // kernel applies: FP16, 16 states, dt_rank a multiple of 8 up to 128,
-    // x_proj rows 16-byte aligned, one 128-channel CTA per SM or more.
-    // MAMBA_DT_FUSE=0 keeps the separate GEMM.
-    bool dt_fuse = true;
+    // dt_proj folded into the scan (selective_scan_dtproj) when
+    // MAMBA_DT_FUSE=1, wherever that kernel applies: FP16, 16 states,
+    // dt_rank a multiple of 8 up to 128, x_proj rows 16-byte aligned, one
+    // 128-channel CTA per SM or more.  Off by default: at the 48-layer
+    // workload the fused scan takes 9.3 ms per layer against 7.4 + 0.66 ms
+    // for the scan and the separate GEMM (the per-tile MMA issue and TMEM
+    // read sit on the path of warps that each carry 32 channels).
+    bool dt_fuse = false;
     bool fuse_dt(const MambaScanArgs &sa) const {
         return dt_fuse && act == MAMBA_F16 && (XD * 2) % 16 == 0 && scan_dtproj_supported(&sa, R);
     }

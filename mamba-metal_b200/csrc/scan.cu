@@ -476,22 +476,28 @@ __global__ void __launch_bounds__(CH, kTmaMinCtas)
 // 16-step tile the TMA ring brings the dt_r tile [16 x dt_rank] (FP16,
 // 128-byte swizzle) in place of the delta tile; one thread issues
 // tcgen05.mma (M 128 channels, N 16 steps, A from TMEM, B from shared
-// memory) into one of three 16-column TMEM accumulators, a tile ahead of
-// its use, and each thread reads its channel's 16 values with tcgen05.ld,
+// memory) into one of three 16-column TMEM accumulators, two tiles ahead
+// of its use, and each thread reads its channel's 16 values with tcgen05.ld,
 // rounds them to FP16 (the values the separate GEMM would store) and writes
 // them over the consumed dt_r tile, where the unchanged recurrence reads
 // them as its delta tile.  Every wait is bounded; TMEM is freed on every
 // path.
 template <int ST>
 struct DtLayout {
-    static constexpr int kXB = kTmaTT * kScanCH * 2;  // x or z tile, FP16
-    static constexpr int kDB = 2 * kTmaTT * 128;      // dt_r: two [16 x 64] FP16 boxes; later the FP16 draw tile
-    static constexpr int kBCB = kTmaTT * 16 * 2;      // B or C tile, FP16
-    static constexpr int kOffD = kXB, kOffZ = kXB + kDB, kOffB = 2 * kXB + kDB, kOffC = kOffB + kBCB;
-    static constexpr int kStage = (kOffC + kBCB + 1023) / 1024 * 1024;  // swizzled boxes need 1 KB alignment
-    static constexpr int kBC = 2 * kTmaTT * 2 * 16 * 4;                // double-buffered FP32 B/C
-    static constexpr int kBytes = 1024 + ST * kStage + kBC + (2 * ST + 1) * 8 + 16;
-    static_assert(kDB == kTmaTT * kScanCH * 2, "the draw tile reuses the dt_r slot");
+    static constexpr int RS = ST + 1;                  // dt_r slots: one tile ahead of the main ring
+    static constexpr int kXB = kTmaTT * kScanCH * 2;   // x or z tile, FP16
+    static constexpr int kBCB = kTmaTT * 16 * 2;       // B or C tile, FP16
+    static constexpr int kOffZ = kXB, kOffB = 2 * kXB, kOffC = kOffB + kBCB;
+    static constexpr int kStage = kOffC + kBCB;        // x | z | B | C
+    static constexpr int kDR = 2 * kTmaTT * 128;       // dt_r: two [16 x 64] FP16 boxes; later the FP16 draw tile
+    static constexpr int kOffDR = 0;                   // dt_r slots first (1 KB aligned for the swizzle)
+    static constexpr int kOffStages = RS * kDR;
+    static constexpr int kBC = 2 * kTmaTT * 2 * 16 * 4;  // double-buffered FP32 B/C
+    static constexpr int kOffBC = kOffStages + ST * kStage;
+    static constexpr int kOffBars = kOffBC + kBC;
+    static constexpr int kBytes = 1024 + kOffBars + (ST + RS + 3 + 1) * 8 + 16;
+    static_assert(kDR == kTmaTT * kScanCH * 2, "the draw tile reuses its dt_r slot");
+    static_assert(kStage % 128 == 0, "TMA destinations stay 128-byte aligned");
 };
 constexpr int kDtMaxRank = 128;
 constexpr int kDtTmemCols = 128;  // W_dt (64 columns) + three 16-column accumulators
@@ -504,12 +510,16 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
                       const __half *__restrict__ wdt, int R) {
     constexpr int NS = 16, CH = kScanCH, TT = kTmaTT;
     using Lay = DtLayout<ST>;
+    constexpr int RS = Lay::RS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *bcf = reinterpret_cast<float *>(smem + ST * Lay::kStage);                  // [2][TT][2*NS]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ST * Lay::kStage + Lay::kBC);  // [ST] copies landed
-    uint64_t *mbars = bars + ST;                                                       // [ST] draw tile in TMEM
-    uint64_t *drain = mbars + ST;
+    uint8_t *dr_slots = smem + Lay::kOffDR;                             // [RS] dt_r boxes / draw tiles
+    uint8_t *stages = smem + Lay::kOffStages;                           // [ST] x | z | B | C
+    float *bcf = reinterpret_cast<float *>(smem + Lay::kOffBC);         // [2][TT][2*NS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lay::kOffBars);  // [ST] main copies landed
+    uint64_t *dbars = bars + ST;                                        // [RS] dt_r copies landed
+    uint64_t *mbars = dbars + RS;                                       // [3] draw accumulator ready
+    uint64_t *drain = mbars + 3;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -520,8 +530,9 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
     const int ntiles = (L + TT - 1) / TT;
     const bool has_z = p.z != nullptr;
     const int nkb = (R + 63) / 64;  // 64-wide K boxes of dt_r (zero past dt_rank)
-    const uint32_t tx_bytes = Lay::kXB + nkb * TT * 128 + (has_z ? Lay::kXB : 0) + 2u * (uint32_t)(N * TT * 2);
-    const uint32_t idesc = idesc_f16_f32acc(128, TT);
+    const uint32_t tx_main = Lay::kXB + (has_z ? Lay::kXB : 0) + 2u * (uint32_t)(N * TT * 2);
+    const uint32_t tx_dr = (uint32_t)(nkb * TT * 128);
+    constexpr uint32_t idesc = idesc_f16_f32acc(128, TT);
 
     float2 Ac[NS / 2], kI[NS / 2], h[NS / 2], P[NS / 2];
     const bool small = load_channel_consts<NS, false>(p.A, d, N, dvalid, Ac, kI);
@@ -537,10 +548,9 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
         if (has_z) prefetch_tensormap(&tmz);
         prefetch_tensormap(&tmB);
         prefetch_tensormap(&tmC);
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(&bars[s], 1);
-            mbar_init(&mbars[s], 1);
-        }
+        for (int s = 0; s < ST; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < RS; ++s) mbar_init(&dbars[s], 1);
+        for (int s = 0; s < 3; ++s) mbar_init(&mbars[s], 1);
         mbar_init(drain, 1);
         fence_mbar_init();
     }
@@ -577,41 +587,51 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
     __syncthreads();
     tc_fence_after();
 
-    auto issue = [&](int tile, int s) {
-        uint8_t *stg = smem + s * Lay::kStage;
+    auto issue = [&](int tile) {
+        const int s = tile % ST;
+        uint8_t *stg = stages + s * Lay::kStage;
         const int t = tile * TT;
-        mbar_arrive_expect_tx(&bars[s], tx_bytes);
+        mbar_arrive_expect_tx(&bars[s], tx_main);
         tma_load_3d(stg, &tmx, &bars[s], d0, t, b);
-        for (int kb = 0; kb < nkb; ++kb) tma_load_3d(stg + Lay::kOffD + kb * TT * 128, &tmdr, &bars[s], kb * 64, t, b);
         if (has_z) tma_load_3d(stg + Lay::kOffZ, &tmz, &bars[s], d0, t, b);
         tma_load_3d(stg + Lay::kOffB, &tmB, &bars[s], 0, t, b);
         tma_load_3d(stg + Lay::kOffC, &tmC, &bars[s], 0, t, b);
     };
-    // One thread: the draw tile of `tile` (stage s) into accumulator s.
-    auto issue_mma = [&](int s) {
+    auto issue_dr = [&](int tile) {
+        const int r = tile % RS;
+        mbar_arrive_expect_tx(&dbars[r], tx_dr);
+        for (int kb = 0; kb < nkb; ++kb)
+            tma_load_3d(dr_slots + r * Lay::kDR + kb * TT * 128, &tmdr, &dbars[r], kb * 64, tile * TT, b);
+    };
+    // One thread: the draw tile of `tile` into accumulator tile % 3, once its
+    // dt_r boxes have landed.
+    auto issue_mma = [&](int tile) -> bool {
+        const int r = tile % RS;
+        if (!mbar_wait_bounded(&dbars[r], (uint32_t)((tile / RS) & 1))) return false;
         tc_fence_after();
-        const uint32_t b_addr = smem_u32(smem + s * Lay::kStage + Lay::kOffD);
-        const uint32_t d_tmem = tmem + 64 + 16 * s;
+        const uint32_t b_addr = smem_u32(dr_slots + r * Lay::kDR);
+        const uint32_t d_tmem = tmem + 64 + 16 * (tile % 3);
         for (int kk = 0; kk < 4 * nkb; ++kk)
             umma_f16_ts(d_tmem, tmem + 8 * kk, smem_desc_sw128(b_addr + (kk >> 2) * TT * 128 + (kk & 3) * 32), idesc,
                         kk != 0);
-        umma_commit(&mbars[s]);
+        umma_commit(&mbars[tile % 3]);
+        return true;
     };
-    auto stage_bc = [&](int s, int t0, float *dst) {
-        const uint8_t *stg = smem + s * Lay::kStage;
+    auto stage_bc = [&](int tile, float *dst) {
+        const uint8_t *stg = stages + (tile % ST) * Lay::kStage;
         convert_bc<NS, CH, TT, __half, false>(reinterpret_cast<const __half *>(stg + Lay::kOffB),
-                                              reinterpret_cast<const __half *>(stg + Lay::kOffC), dst, N, t0, L);
+                                              reinterpret_cast<const __half *>(stg + Lay::kOffC), dst, N, tile * TT,
+                                              L);
     };
-    if (tid == 0)
-        for (int s = 0; s < min(ST, ntiles); ++s) issue(s, s);
-
     bool ok0 = true;
+    if (tid == 0) {
+        for (int t = 0; t < min(RS, ntiles); ++t) issue_dr(t);
+        for (int t = 0; t < min(ST, ntiles); ++t) issue(t);
+        for (int t = 0; t < min(2, ntiles); ++t) ok0 = ok0 && issue_mma(t);
+    }
     if (ntiles > 0) {
-        ok0 = mbar_wait_bounded(&bars[0], 0u);
-        if (ok0) {
-            if (tid == 0) issue_mma(0);
-            stage_bc(0, 0, bcf);
-        }
+        ok0 = ok0 && mbar_wait_bounded(&bars[0], 0u);
+        if (ok0) stage_bc(0, bcf);
     }
     int i = 0;
     bool aborted = __syncthreads_or(!ok0);
@@ -619,29 +639,20 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
         const int s = i % ST;
         const int t0 = i * TT;
         const int nt = min(TT, L - t0);
-        const uint32_t ph = (uint32_t)((i / ST) & 1);
-        bool ok = true;
-        // the next tile's draw is computed while this one is scanned
-        if (tid == 0 && i + 1 < ntiles) {
-            const int s1 = (i + 1) % ST;
-            if (mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1)))
-                issue_mma(s1);
-            else
-                ok = false;
-        }
-        ok = ok && mbar_wait_bounded(&bars[s], ph) && mbar_wait_bounded(&mbars[s], ph);
+        bool ok = mbar_wait_bounded(&bars[s], (uint32_t)((i / ST) & 1)) &&
+                  mbar_wait_bounded(&mbars[i % 3], (uint32_t)((i / 3) & 1));
         ok = __all_sync(0xffffffffu, ok);  // the TMEM load below is warp-collective
-        uint8_t *stg = smem + s * Lay::kStage;
         if (ok) {
             tc_fence_after();
             uint32_t v[16];
-            tmem_ld_32x32b_x16(tmem + lane_base + 64 + 16 * s, v);
+            tmem_ld_32x32b_x16(tmem + lane_base + 64 + 16 * (i % 3), v);
             tmem_wait_ld();
             // over the consumed dt_r boxes: this thread's column of the FP16 draw tile
-            __half *sD = reinterpret_cast<__half *>(stg + Lay::kOffD);
+            __half *sD = reinterpret_cast<__half *>(dr_slots + (i % RS) * Lay::kDR);
 #pragma unroll
             for (int tt = 0; tt < TT; ++tt) sD[tt * CH + tid] = __float2half_rn(__uint_as_float(v[tt]));
             if (dvalid) {
+                const uint8_t *stg = stages + s * Lay::kStage;
                 const __half *sX = reinterpret_cast<const __half *>(stg);
                 const __half *sZ = reinterpret_cast<const __half *>(stg + Lay::kOffZ);
                 const float *sBC = bcf + (i & 1) * TT * 2 * NS;
@@ -655,12 +666,13 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
         }
         if (i + 1 < ntiles) {
             float *next = bcf + ((i + 1) & 1) * TT * 2 * NS;
-            const int s1 = (i + 1) % ST;
-            const bool ok1 = mbar_wait_bounded(&bars[s1], (uint32_t)(((i + 1) / ST) & 1));
-            if (ok1) stage_bc(s1, t0 + TT, next);
+            const bool ok1 = mbar_wait_bounded(&bars[(i + 1) % ST], (uint32_t)(((i + 1) / ST) & 1));
+            if (ok1) stage_bc(i + 1, next);
             ok = ok && ok1;
         }
-        // the stage's shared memory is overwritten by the next copies
+        // two tiles ahead: its dt_r boxes were issued two tiles ago
+        if (tid == 0 && i + 2 < ntiles) ok = ok && issue_mma(i + 2);
+        // the stage, the draw tile and this tile's accumulator are reused next
         fence_proxy_async_smem();
         tc_fence_before();
         if (__syncthreads_or(!ok)) {
@@ -668,7 +680,10 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
             break;
         }
         tc_fence_after();
-        if (tid == 0 && i + ST < ntiles) issue(i + ST, s);
+        if (tid == 0) {
+            if (i + ST < ntiles) issue(i + ST);
+            if (i + RS < ntiles) issue_dr(i + RS);
+        }
     }
     if (tid == 0) {
         // every issued MMA has finished before TMEM is freed
@@ -676,8 +691,9 @@ __global__ void __launch_bounds__(kScanCH, kTmaMinCtas)
         if (!mbar_wait_bounded(drain, 0u)) aborted = true;
         if (aborted) {
             atomicOr(&g_device_error, kErrTmaTimeout);
-            for (int j = i; j < min(i + ST, ntiles); ++j)
-                mbar_wait_bounded(&bars[j % ST], (uint32_t)((j / ST) & 1));
+            // copies still landing in this CTA's shared memory finish first
+            for (int j = i; j < min(i + ST, ntiles); ++j) mbar_wait_bounded(&bars[j % ST], (uint32_t)((j / ST) & 1));
+            for (int j = i; j < min(i + RS, ntiles); ++j) mbar_wait_bounded(&dbars[j % RS], (uint32_t)((j / RS) & 1));
         }
     }
     tc_fence_before();

@@ -70,9 +70,10 @@ def test_dtproj_scan_rejects_unsupported_shapes(cuda):
 
 
 def test_model_forward_with_dt_fused_scan(cuda, monkeypatch):
-    """A layer shape where the model folds dt_proj into the scan (d_inner
-    2048 x batch 10 = 160 channel CTAs): the forward matches the forward
-    with the separate GEMM (MAMBA_DT_FUSE=0) and the CPU block reference."""
+    """A layer shape where the model can fold dt_proj into the scan (d_inner
+    2048 x batch 10 = 160 channel CTAs), with MAMBA_DT_FUSE=1: the forward
+    matches the forward with the separate GEMM (the default) and the CPU
+    block reference."""
     rng = np.random.default_rng(120)
     cfg = mb.MambaConfig(1024, 16, 4, 2, 1, mb.F16)
     layers = [mb.random_layer_weights(cfg, rng)]
