@@ -67,6 +67,41 @@ __device__ __forceinline__ float rcp_newton2(float v) {
     return r;
 }
 
+// 2^v on the FMA pipe instead of the special-function unit: Cody-Waite
+// reduction v = j + f (j = round(v) by the 1.5 * 2^23 magic add, |f| <= 1/2),
+// 2^f = 1 + f q(f) with q interpolating (2^f - 1)/f at the five Chebyshev
+// nodes of [-1/2, 1/2] (coefficients computed here in FP64, rounded to FP32;
+// max relative error of the FP32 evaluation 2.6e-7), and j added to the
+// exponent field as an integer.  v is clamped to [-125, 127], so the result
+// stays a normal number (2^-125 where ex2.approx.ftz would flush to 0).
+__device__ __forceinline__ float ex2_fma(float v) {
+    v = fminf(fmaxf(v, -125.f), 127.f);
+    const float t = v + 12582912.f;
+    const float f = v - (t - 12582912.f);
+    float q = 1.338130212e-03f;
+    q = fmaf(q, f, 9.666368365e-03f);
+    q = fmaf(q, f, 5.550381169e-02f);
+    q = fmaf(q, f, 2.402234972e-01f);
+    q = fmaf(q, f, 6.931471825e-01f);
+    const float p = fmaf(q, f, 1.f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+#ifndef MAMBA_SCAN_FMA_EXP
+#define MAMBA_SCAN_FMA_EXP 0
+#endif
+// State exponentials of the one-thread scan's fast path: the last state of
+// each channel on the FMA pipe (ex2_fma) when built with
+// MAMBA_SCAN_FMA_EXP=1, else all on the special-function unit.  Off by
+// default: with it the scan of batch 64 x L 4096 x 4096 channels took 6.16 ms
+// against 5.90 (the FMA pipe and issue slots, already ~55-60% busy, became
+// the limit).  The decode kernels and the four-lane scan always use
+// ex2.approx, so with the flag set their states no longer equal the scan's
+// bit for bit.
+__device__ __forceinline__ float state_ex2(float v, bool last_state) {
+    return (MAMBA_SCAN_FMA_EXP && last_state) ? ex2_fma(v) : ex2_approx(v);
+}
+
 // SiLU(z) = z / (1 + exp(-z)) with one ex2 and a Newton reciprocal.
 __device__ __forceinline__ float silu_fast(float z) {
     return z * rcp_newton2(1.f + ex2_approx(fminf(-z * kLog2e, 120.f)));
@@ -175,7 +210,7 @@ __device__ __forceinline__ float scan_step(float xv, float dt, const float *__re
                 a.y = expf(dA.y);
             } else {
                 a.x = ex2_approx(dA.x);
-                a.y = ex2_approx(dA.y);
+                a.y = state_ex2(dA.y, p == NS / 2 - 1);
             }
             const float2 w = __fmul2_rn(x2, Bp);
             if (SMALLA) {
