@@ -472,12 +472,22 @@ struct Model {
         MB_CHECK_ARG(in && out, "forward: null pointer");
         if (!st) st = cur_stream();
         if (in != out) MB_CUDA_TRY(cudaMemcpyAsync(out, in, sizeof(float) * T * M, cudaMemcpyDeviceToDevice, st));
+        return forward_layers(out, batch, L, 0, (int)layers.size(), st);
+    }
+
+    // Layers [l0, l1) on the FP32 residual stream out [batch, L, M], in place.
+    // Every op is independent across batch rows, so a row range run alone
+    // gives the same bits as inside the whole batch (as long as both take the
+    // same kernels: more than 512 rows per GEMM).
+    int forward_layers(float *out, int batch, int L, int l0, int l1, cudaStream_t st) {
+        const int64_t T = (int64_t)batch * L;
         Arena ar{};
         if (ensure_arena(batch, L, ar)) return -1;
         const int64_t Ld = L;
         const int64_t xs[3] = {Ld * 2 * D, 2 * D, 1};
         const int64_t us[3] = {Ld * D, D, 1};
-        for (const LayerWeights &w : layers) {
+        for (int li = l0; li < l1; ++li) {
+            const LayerWeights &w = layers[li];
             {
                 OpScope o(prof, MAMBA_OP_RMSNORM, st, 1);
                 if (rmsnorm(out, w.norm_w, ar.normed, T, M, kNormEps, MAMBA_F32, act, st)) return -1;
@@ -536,11 +546,21 @@ struct Model {
         return 0;
     }
 
-    // Host-buffer forward.  Large inputs are cut into row chunks: chunk k+1
-    // is uploaded and chunk k-1 downloaded on copy streams while chunk k is
-    // computed, so the PCIe transfers hide behind the layers (overlap needs
-    // pinned host memory; pageable buffers are staged by the driver).
+    // Host-buffer forward.  Large inputs are cut into row chunks uploaded and
+    // downloaded on copy streams while other rows compute, so the PCIe
+    // transfers hide behind the layers (overlap needs pinned host memory;
+    // pageable buffers are staged by the driver).  With at least
+    // 2 * kEdgeLayers layers the row chunks (batch/8 rows each) only drive
+    // the edge layers: the first kEdgeLayers layers run per chunk as its
+    // upload lands, the layers between run once on the whole batch, and the
+    // last kEdgeLayers run per chunk, each chunk's download issued as soon as
+    // it is done.  Only the first chunk's upload and the last chunk's
+    // download are exposed, and only the edge layers run at the chunk's
+    // smaller batch (whose scan fills fewer SMs).  Shallower stacks (and
+    // forced chunk counts, MAMBA_HOST_CHUNKS) run whole-stack forwards over
+    // the chunks: [c, batch - 2c, c] rows, c ~ batch/8.
     static constexpr size_t kChunkedHostBytes = 64u << 20;
+    static constexpr int kEdgeLayers = 2;
     int host_chunks = 0;  // MAMBA_HOST_CHUNKS: forced chunk count (0 = automatic)
     cudaStream_t h2d = nullptr, d2h = nullptr;
     std::vector<cudaEvent_t> io_events;
@@ -566,13 +586,17 @@ struct Model {
         }
         if (!h2d) MB_CUDA_TRY(cudaStreamCreateWithFlags(&h2d, cudaStreamNonBlocking));
         if (!d2h) MB_CUDA_TRY(cudaStreamCreateWithFlags(&d2h, cudaStreamNonBlocking));
-        // Row ranges: forced chunk counts split evenly; the automatic split is
-        // [c, batch - 2c, c] with c ~ batch/8, so only the short first upload
-        // and the short last download are exposed.
+        // Row ranges: forced chunk counts split evenly; automatic: batch/8
+        // rows per chunk for the edge-layer schedule, else [c, batch - 2c, c].
+        const int nl = (int)layers.size();
+        const bool edges = host_chunks == 0 && batch >= 3 && nl >= 2 * kEdgeLayers;
         std::vector<int> starts;
         if (host_chunks > 0 || batch < 3) {
             const int rows = (batch + chunks - 1) / chunks;
             for (int r0 = 0; r0 < batch; r0 += rows) starts.push_back(r0);
+        } else if (edges) {
+            const int c = std::max(1, batch / 8);
+            for (int r0 = 0; r0 < batch; r0 += c) starts.push_back(r0);
         } else {
             const int c = std::max(1, batch / 8);
             starts = {0, c, batch - c};
@@ -605,22 +629,45 @@ struct Model {
             if (!err) note(cudaEventRecord(io_events[2 * k], h2d), "event record");
             if (!err) uploaded = k + 1;
         }
-        for (int k = 0; k < uploaded && !err; ++k) {
+        // Compute on st; chunk k's download waits for the event after its
+        // last layer.
+        auto download = [&](int k) {
             const int r0 = starts[k], nr = starts[k + 1] - r0;
-            if (nr <= 0) break;
-            float *dk = d + r0 * row_elems;
-            note(cudaStreamWaitEvent(st, io_events[2 * k], 0), "stream wait");
-            if (err) break;
-            if (forward_device(dk, dk, nr, L, st)) {
-                err = -1;
-                break;
-            }
             note(cudaEventRecord(io_events[2 * k + 1], st), "event record");
             if (!err) note(cudaStreamWaitEvent(d2h, io_events[2 * k + 1], 0), "stream wait");
             if (!err)
-                note(cudaMemcpyAsync(out + r0 * row_elems, dk, sizeof(float) * nr * row_elems,
+                note(cudaMemcpyAsync(out + r0 * row_elems, d + r0 * row_elems, sizeof(float) * nr * row_elems,
                                      cudaMemcpyDeviceToHost, d2h),
                      "device-to-host copy");
+        };
+        if (edges) {
+            // The arena at full size first, so no chunk call regrows it.
+            Arena full{};
+            if (uploaded < chunks || ensure_arena(batch, L, full)) err = -1;
+            for (int k = 0; k < chunks && !err; ++k) {
+                const int r0 = starts[k], nr = starts[k + 1] - r0;
+                note(cudaStreamWaitEvent(st, io_events[2 * k], 0), "stream wait");
+                if (!err && forward_layers(d + r0 * row_elems, nr, L, 0, kEdgeLayers, st)) err = -1;
+            }
+            if (!err && forward_layers(d, batch, L, kEdgeLayers, nl - kEdgeLayers, st)) err = -1;
+            for (int k = 0; k < chunks && !err; ++k) {
+                const int r0 = starts[k], nr = starts[k + 1] - r0;
+                if (forward_layers(d + r0 * row_elems, nr, L, nl - kEdgeLayers, nl, st)) err = -1;
+                if (!err) download(k);
+            }
+        } else {
+            for (int k = 0; k < uploaded && !err; ++k) {
+                const int r0 = starts[k], nr = starts[k + 1] - r0;
+                if (nr <= 0) break;
+                float *dk = d + r0 * row_elems;
+                note(cudaStreamWaitEvent(st, io_events[2 * k], 0), "stream wait");
+                if (err) break;
+                if (forward_device(dk, dk, nr, L, st)) {
+                    err = -1;
+                    break;
+                }
+                download(k);
+            }
         }
         const cudaError_t e1 = cudaStreamSynchronize(h2d);
         const cudaError_t e2 = cudaStreamSynchronize(st);

@@ -235,6 +235,26 @@ def test_chunked_host_forward_matches_device_forward(cuda, monkeypatch):
     assert oracle.normwise_rel_err(out - h, ref_cpu - h) < 2e-3
 
 
+def test_edge_layer_host_forward_is_bitwise_the_device_forward(cuda):
+    """A 4-layer stack with a 84 MB host input: mamba_forward runs the first
+    and last two layers per row chunk (5 rows, uploads and downloads
+    overlapped) and the middle layers on the whole batch.  Every op is
+    row-independent and the chunks take the same kernels as the whole batch
+    here (over 512 rows per GEMM, at least one 128-channel scan CTA per SM),
+    so the output equals the single-call device forward bit for bit."""
+    m = mb.Model(2048, 16, 4, 2, 4, mb.F16)
+    m.init_random(11)
+    h = np.random.default_rng(110).standard_normal((40, 256, 2048)).astype(np.float32)
+    out = m.forward(h)
+    dh = torch.from_numpy(h).cuda()
+    dout = torch.empty_like(dh)
+    m.forward_device(dh.data_ptr(), dout.data_ptr(), 40, 256)
+    torch.cuda.synchronize()
+    assert mb.device_status() == 0
+    assert np.array_equal(out, dout.cpu().numpy())
+    assert not np.array_equal(out, h)
+
+
 def test_save_weights_round_trip(cuda):
     """mamba_save_weights writes a blob that reproduces the model bit for bit
     when loaded into a second model; its projections are the FP16 values the
