@@ -206,12 +206,13 @@ def test_ssm_step_multirow_kernel(cuda, misalign):
     assert err(st, st_ref) < TOL32
 
 
-def test_ssm_step_bulk_copy_kernel(cuda):
-    """Enough 32-channel x 16-row blocks to take the bulk-copy FP16 decode
-    kernel (3072 channels x batch 40: the last row block holds 8 rows): the
+@pytest.mark.parametrize("bsz", [40, 42])
+def test_ssm_step_bulk_copy_kernel(cuda, bsz):
+    """Enough 32-channel x 4-row blocks to take the bulk-copy FP16 decode
+    kernel (3072 channels; batch 42 leaves a last row group of 2): the
     outputs match the oracle step, and T steps leave exactly the scan's final
     state (the per-state operations are the scan's)."""
-    bsz, L, D, N = 40, 6, 3072, 16
+    L, D, N = 6, 3072, 16
     x, dr, B, C, z, A, Dk = scan_inputs(23, bsz, L, D, N)
     x, dr, B, C, z = map(r16, (x, dr, B, C, z))
     bias = np.random.default_rng(2).normal(0, 0.5, D).astype(np.float32)
