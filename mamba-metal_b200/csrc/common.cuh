@@ -17,6 +17,13 @@ void set_error(const std::string &msg);
 const char *last_error();
 void clear_error();
 
+// ---- logging ----------------------------------------------------------------
+// Lines "mamba-b200: ..." on stderr when the environment variable MAMBA_LOG
+// is at least `level`: 0 (default) silent, 1 errors (every set_error), 2
+// model set-up and graph captures, 3 one line per forward / step call.
+int log_level();
+void log_msg(int level, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
 #define MB_CUDA_TRY(expr)                                                          \
     do {                                                                           \
         cudaError_t _e = (expr);                                                   \

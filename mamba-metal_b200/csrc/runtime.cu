@@ -18,7 +18,11 @@
 // The residual stream h stays FP32; activations use cfg.dtype.
 #include <cublas_v2.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cmath>
+#include <cstdarg>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -35,7 +39,26 @@ namespace mb {
 namespace {
 thread_local std::string g_last_error;
 }
-void set_error(const std::string &msg) { g_last_error = msg; }
+int log_level() {
+    static const int level = [] {
+        const char *e = std::getenv("MAMBA_LOG");
+        return e ? std::max(0, std::atoi(e)) : 0;
+    }();
+    return level;
+}
+void log_msg(int level, const char *fmt, ...) {
+    if (log_level() < level) return;
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    std::fprintf(stderr, "mamba-b200: %s\n", buf);
+}
+void set_error(const std::string &msg) {
+    g_last_error = msg;
+    log_msg(1, "error: %s", msg.c_str());
+}
 const char *last_error() { return g_last_error.c_str(); }
 void clear_error() { g_last_error.clear(); }
 
@@ -120,6 +143,12 @@ struct LayerWeights {
 // pool that is reused after every mamba_profile_enable.
 struct Profiler {
     bool on = false;
+    // MAMBA_DEBUG=1: every operation's stream is synchronised and checked
+    // (CUDA error, device status flags) right after it; the first failure
+    // names the operation and layer and makes the call return -1.
+    bool debug = false;
+    bool debug_failed = false;
+    int layer = -1;
     std::vector<cudaEvent_t> pool;
     size_t used = 0;
     struct Rec {
@@ -145,7 +174,14 @@ struct Profiler {
     }
 };
 
-// Brackets one operation with an event pair while profiling is on.
+const char *op_name(int op) {
+    static const char *names[MAMBA_OP_COUNT] = {"rmsnorm", "in_proj", "conv", "x_proj",
+                                                "dt_proj", "scan",    "out_proj"};
+    return op >= 0 && op < MAMBA_OP_COUNT ? names[op] : "op";
+}
+
+// Brackets one operation: an NVTX range named after it, an event pair while
+// profiling is on, and the MAMBA_DEBUG check after it.
 struct OpScope {
     Profiler &p;
     int op;
@@ -153,12 +189,43 @@ struct OpScope {
     int kernels;  // this library's kernels in the operation (may be set after construction)
     cudaEvent_t a = nullptr;
     OpScope(Profiler &p_, int op_, cudaStream_t s, int k) : p(p_), op(op_), st(s), kernels(k) {
+        nvtxRangePushA(op_name(op));
         if (p.on && (a = p.take())) cudaEventRecord(a, st);
     }
     ~OpScope() {
+        nvtxRangePop();
+        if (p.debug && !p.debug_failed) debug_check();
         if (!p.on || !a) return;
         cudaEvent_t b = p.take();
         if (b && cudaEventRecord(b, st) == cudaSuccess) p.recs.push_back({op, a, b, kernels});
+    }
+    void debug_check() {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+        const cudaError_t e1 = cudaStreamSynchronize(st);
+        const cudaError_t e2 = cudaGetLastError();
+        const unsigned flags = mamba_device_status(0);
+        if (e1 == cudaSuccess && e2 == cudaSuccess && flags == 0) return;
+        p.debug_failed = true;
+        char buf[256];
+        std::snprintf(buf, sizeof(buf), "MAMBA_DEBUG: operation %s of layer %d failed: %s (device status 0x%x)",
+                      op_name(op), p.layer, cudaGetErrorString(e1 != cudaSuccess ? e1 : e2), flags);
+        set_error(buf);
+    }
+};
+
+// NVTX range over one layer; also tells the debug check which layer runs.
+struct LayerScope {
+    Profiler &p;
+    LayerScope(Profiler &p_, int l) : p(p_) {
+        p.layer = l;
+        char name[32];
+        std::snprintf(name, sizeof(name), "mamba layer %d", l);
+        nvtxRangePushA(name);
+    }
+    ~LayerScope() {
+        nvtxRangePop();
+        p.layer = -1;
     }
 };
 
@@ -259,6 +326,12 @@ struct Model {
         if (const char *pj = std::getenv("MAMBA_PROJ")) proj_tc = std::atoi(pj) != 0;
         if (const char *cf = std::getenv("MAMBA_CONV_FUSE")) conv_fuse = std::atoi(cf) != 0;
         if (const char *df = std::getenv("MAMBA_DT_FUSE")) dt_fuse = std::atoi(df) != 0;
+        if (const char *dbg = std::getenv("MAMBA_DEBUG")) prof.debug = std::atoi(dbg) != 0;
+        log_msg(2, "model on device %d (%s, %d SMs): d_model %d, d_inner %d, d_state %d, d_conv %d, dt_rank %d, "
+                   "%d layers, %s activations; projections on %s; debug checks %s",
+                dev, prop.name, prop.multiProcessorCount, M, D, N, K, R, c.n_layer, act == MAMBA_F16 ? "FP16" : "FP32",
+                proj_tc && act == MAMBA_F16 ? "the CTA-pair tcgen05 GEMM (> 512 rows)" : "cuBLAS",
+                prof.debug ? "on" : "off");
         if (cublasCreate(&cublas) != CUBLAS_STATUS_SUCCESS) {
             set_error("cublasCreate failed");
             return -1;
@@ -486,7 +559,10 @@ struct Model {
         const int64_t Ld = L;
         const int64_t xs[3] = {Ld * 2 * D, 2 * D, 1};
         const int64_t us[3] = {Ld * D, D, 1};
+        prof.debug_failed = false;
         for (int li = l0; li < l1; ++li) {
+            if (prof.debug_failed) return -1;
+            LayerScope layer_scope(prof, li);
             const LayerWeights &w = layers[li];
             {
                 OpScope o(prof, MAMBA_OP_RMSNORM, st, 1);
@@ -543,7 +619,7 @@ struct Model {
                 o.kernels = last_gemm_kernels;
             }
         }
-        return 0;
+        return prof.debug_failed ? -1 : 0;
     }
 
     // Host-buffer forward.  Large inputs are cut into row chunks uploaded and
@@ -577,6 +653,8 @@ struct Model {
         float *d = static_cast<float *>(io.ptr);
         int chunks = host_chunks > 0 ? host_chunks : (bytes >= kChunkedHostBytes ? 2 : 1);
         chunks = std::max(1, std::min(chunks, batch));
+        log_msg(3, "forward: batch %d x L %d from host buffers (%zu bytes each way), %s", batch, L, bytes,
+                chunks == 1 ? "one call" : "row chunks overlapped with the copies");
         if (chunks == 1) {
             MB_CUDA_TRY(cudaMemcpyAsync(d, in, bytes, cudaMemcpyHostToDevice, st));
             if (forward_device(d, d, batch, L, st)) return -1;
@@ -745,7 +823,10 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
     const size_t a = m.act_size();
     const int D = m.D, N = m.N, K = m.K, R = m.R, XD = m.XD;
     Profiler &pf = m.prof;
+    pf.debug_failed = false;
     for (int l = 0; l < m.cfg.n_layer; ++l) {
+        if (pf.debug_failed) return -1;
+        LayerScope layer_scope(pf, l);
         const LayerWeights &w = m.layers[l];
         float *conv_state = s.conv + (size_t)l * Bt * D * (K - 1);
         float *ssm_state = s.ssm + (size_t)l * Bt * D * N;
@@ -793,7 +874,7 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
             o.kernels = m.last_gemm_kernels;
         }
     }
-    return 0;
+    return pf.debug_failed ? -1 : 0;
 }
 
 static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *out, cudaStream_t st) {
@@ -809,12 +890,15 @@ static int step_device(Model &m, MambaStateHandle &s, const float *tok, float *o
     MB_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
     // Plain launches when graphs are off, while profiling (events per
     // operation), or when the caller is capturing the stream itself.
-    if (!m.use_graphs || m.prof.on || cs != cudaStreamCaptureStatusNone) return step_enqueue(m, s, tok, out, st, ar);
+    log_msg(3, "step: batch %d, %d layers", Bt, m.cfg.n_layer);
+    if (!m.use_graphs || m.prof.on || m.prof.debug || cs != cudaStreamCaptureStatusNone)
+        return step_enqueue(m, s, tok, out, st, ar);
     StepGraph &g = m.step_graph;
     const bool hit = g.exec && g.conv == s.conv && g.ssm == s.ssm && g.batch == Bt && g.in == tok && g.out == out &&
                      g.st == st && g.arena == m.step_arena.ptr;
     if (!hit) {
         g.reset();
+        log_msg(2, "step: capturing the %d-layer decode step as a CUDA graph (batch %d)", m.cfg.n_layer, Bt);
         MB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         const int rc = step_enqueue(m, s, tok, out, st, ar);
         cudaGraph_t graph = nullptr;

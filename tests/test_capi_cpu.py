@@ -145,3 +145,31 @@ def test_create_without_gpu_fails_cleanly():
     cfg = mb.MambaConfig(64, 16, 4, 2, 1, 1)
     assert mb.lib().mamba_create(ctypes.byref(cfg)) is None
     assert mb.last_error() != ""
+
+
+_LOG_PROBE = """
+import ctypes, mamba_b200 as mb
+cfg = mb.MambaConfig(0, 16, 4, 2, 1, mb.F16)  # d_model 0: rejected before any CUDA call
+assert mb.lib().mamba_create(ctypes.byref(cfg)) is None
+print(mb.last_error())
+"""
+
+
+@pytest.mark.parametrize("level", [None, "1"])
+def test_mamba_log_levels(level):
+    """MAMBA_LOG >= 1 copies every error onto stderr as one line prefixed
+    'mamba-b200:' (the reference's 'mamba-metal:' one-liners); unset, the
+    library writes nothing."""
+    env = dict(os.environ)
+    env.pop("MAMBA_LOG", None)
+    if level:
+        env["MAMBA_LOG"] = level
+    env["PYTHONPATH"] = os.path.join(ROOT, "mamba-metal_b200") + os.pathsep + env.get("PYTHONPATH", "")
+    r = subprocess.run(["python", "-c", _LOG_PROBE], capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "mamba_create" in r.stdout
+    lines = [l for l in r.stderr.splitlines() if l.startswith("mamba-b200:")]
+    if level:
+        assert len(lines) == 1 and "error: mamba_create:" in lines[0]
+    else:
+        assert lines == []

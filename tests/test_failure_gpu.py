@@ -45,3 +45,32 @@ def test_selftest_rejects_bad_limits(cuda):
     assert L.mamba_selftest_bounded_wait(0, None) == -1
     assert L.mamba_selftest_bounded_wait(2000000, None) == -1
     assert "limit" in mb.last_error()
+
+
+def test_debug_mode_names_the_failing_operation(cuda, monkeypatch):
+    """MAMBA_DEBUG=1 synchronises and checks the stream after every
+    operation.  With a clean device the debug-mode forward equals the normal
+    one; with a status flag left set (by the bounded-wait self-test, no
+    fault) the first checked operation reports it, and the call fails naming
+    rmsnorm of layer 0; once the flag is cleared the model works again."""
+    rng = np.random.default_rng(3)
+    cfg = mb.MambaConfig(64, 16, 4, 2, 2, mb.F16)
+    layers = [mb.random_layer_weights(cfg, rng) for _ in range(2)]
+    blob = mb.make_weight_blob(cfg, layers)
+    h = rng.standard_normal((2, 40, 64)).astype(np.float32)
+    plain = mb.Model(64, 16, 4, 2, 2, mb.F16)
+    plain.load_weights(blob)
+    ref = plain.forward(h)
+    monkeypatch.setenv("MAMBA_DEBUG", "1")
+    m = mb.Model(64, 16, 4, 2, 2, mb.F16)
+    m.load_weights(blob)
+    L = mb.lib()
+    L.mamba_device_status(1)
+    assert np.array_equal(m.forward(h), ref)
+    st = m.create_state(2)
+    st.step(h[:, 0])  # the decode step runs checked too (no graph in debug mode)
+    assert L.mamba_selftest_bounded_wait(20000, None) == 0
+    with pytest.raises(mb.MambaError, match="MAMBA_DEBUG: operation rmsnorm of layer 0"):
+        m.forward(h)
+    L.mamba_device_status(1)
+    assert np.array_equal(m.forward(h), ref)
