@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -240,6 +241,13 @@ bool encode_kmajor(CUtensorMap *m, const void *ptr, int64_t rows, int cols) {
 int gated_mlp_up(const void *x, const void *w, void *out, int64_t T, int d, int h, cudaStream_t st) {
     MB_CHECK_ARG(T >= 0 && d > 0 && h > 0, "gated_mlp_up: bad sizes");
     if (T == 0) return 0;
+    // The CTA-pair projection GEMM with a SwiGLU epilogue (gemm_tc.cu) is the
+    // default; MAMBA_MLP_PAIR=0 selects this file's one-CTA kernel.
+    static const bool pair = [] {
+        const char *e = std::getenv("MAMBA_MLP_PAIR");
+        return !e || std::atoi(e) != 0;
+    }();
+    if (pair) return proj_gemm_gated(x, w, out, T, d, h, st);
     MB_CHECK_ARG(x && w && out, "gated_mlp_up: null pointer");
     MB_CHECK_ARG(d % 8 == 0 && h % 8 == 0, "gated_mlp_up: d and h must be multiples of 8");
     MB_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&

@@ -93,6 +93,7 @@ struct ProjParams {
     int halo;        // rows each CTA computes ahead of its first output row (3 when the conv is fused)
     int L;           // conv-fused: sequence length (the conv restarts at every multiple of L)
     int x_tiles;     // conv-fused: column tiles 0..x_tiles-1 hold the conv input x, the rest z
+    int up_row0;     // gated (SwiGLU): first W row of the up projection (h); 0 otherwise
     uint32_t idesc;
     uint32_t tx_bytes;  // operand bytes of one stage, both CTAs
 };
@@ -233,7 +234,10 @@ __global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
                 const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
                 // may be negative for the first tile (the halo): those rows read zeros
                 const int arow = mt * 2 * rstep + (int)rank * rstep - p.halo;
-                const int brow = nt * p.BN + (int)rank * half;
+                // gated: the even CTA loads the tile's 128 gate rows, the odd
+                // one the matching 128 up rows, so accumulator columns 0..127
+                // are gate and 128..255 up for the same 128 outputs
+                const int brow = p.up_row0 ? (rank ? p.up_row0 : 0) + nt * half : nt * p.BN + (int)rank * half;
                 for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
                     const uint32_t s = it % kPStages, ph = (it / kPStages) & 1;
                     if (!mbar_wait_bounded(&empty[s], ph ^ 1)) {
@@ -298,8 +302,10 @@ __global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
         const int srow = lane - skip;  // this lane's row in the staged box (< 0: not stored)
         uint8_t *boxes = epi + (warp - 2) * 2 * kPEpiBox;  // this warp's two staging boxes
         const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+        const bool gated = !CONV && p.up_row0 != 0;
         const bool f16 = p.mode == kProjF16;
         const int cstep = f16 ? 64 : 32;
+        const int ccols = gated ? p.BN / 2 : p.BN;  // output columns of a tile
         uint32_t tcount = 0, nbox = 0, nchunk = 0;
         for (int tile = pair; tile < tiles; tile += npairs, ++tcount) {
             const uint32_t b = tcount & 1, tph = (tcount >> 1) & 1;
@@ -314,11 +320,11 @@ __global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
             const int wrow = mt * 2 * rstep + (int)rank * rstep - p.halo + quarter * 32;  // this warp's first row
             const int out_row = wrow + skip;                                                // first stored row
             const bool conv_tile = CONV && nt < p.x_tiles;
-            const int ncol = CONV ? (conv_tile ? nt : nt - p.x_tiles) * p.BN : nt * p.BN;
+            const int ncol = CONV ? (conv_tile ? nt : nt - p.x_tiles) * p.BN : nt * ccols;
             const CUtensorMap *mfull = (CONV && !conv_tile) ? &map_z : &map_c;
             const CUtensorMap *mshort = (CONV && !conv_tile) ? &map_z_short : &map_c_short;
             const CUtensorMap *mstore = skip ? mshort : mfull;
-            const int ncols = CONV ? p.N / 2 : p.N;  // columns of the tensor being stored
+            const int ncols = (CONV || gated) ? p.N / 2 : p.N;  // columns of the tensor being stored
             // sequence position of this warp's first row (the conv restarts
             // at t = 0; halo rows before the first token count as t < 0)
             int tpos0 = 0;
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
             // for the others rows -3..31
             const bool fast_rows = quarter == 0 ? (p.L >= 32 && tpos0 + 31 < p.L) : (tpos0 >= 3 && tpos0 + 31 < p.L);
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + b * kPAccCols;
-            for (int c = egroup * cstep; c < p.BN; c += kGroups * cstep) {
+            for (int c = egroup * cstep; c < ccols; c += kGroups * cstep) {
                 const int col = ncol + c;
                 uint32_t v0[32];
                 uint32_t pk[32];  // FP16 output: 64 columns as 32 packed pairs
@@ -391,6 +397,21 @@ __global__ void __launch_bounds__(ProjCfg<CONV>::kThreads, 1)
                     }
                     ++nbox;
                     continue;
+                } else if (!CONV && gated) {
+                    // silu(gate) * up, 32 outputs at a time (gate at column
+                    // c, up at column 128 + c of the accumulator)
+#pragma unroll
+                    for (int hlf = 0; hlf < 2; ++hlf) {
+                        uint32_t g[32];
+                        tmem_ld_32x32b_x32(tl + c + 32 * hlf, g);
+                        tmem_ld_32x32b_x32(tl + ccols + c + 32 * hlf, v0);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            pk[16 * hlf + j] = pack_half2f(silu_fast(__uint_as_float(g[2 * j])) * __uint_as_float(v0[2 * j]),
+                                                           silu_fast(__uint_as_float(g[2 * j + 1])) *
+                                                               __uint_as_float(v0[2 * j + 1]));
+                    }
                 } else {
                     uint32_t v1[32];
                     tmem_ld_32x32b_x32(tl + c, v0);
@@ -593,6 +614,41 @@ int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void
                           : encode_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, M, N, ldc, 32, 32));
     MB_CHECK_ARG(enc_ok, "proj_gemm: tensor map encoding failed");
     maps[3] = maps[4] = maps[5] = maps[2];  // no halo, no second output
+    return launch_proj<false>(maps, p, st);
+}
+
+int proj_gemm_gated(const void *x, const void *w, void *out, int64_t T, int d, int h, cudaStream_t st) {
+    MB_CHECK_ARG(T >= 0 && d > 0 && h > 0, "gated_mlp_up: bad sizes");
+    if (T == 0) return 0;
+    MB_CHECK_ARG(x && w && out, "gated_mlp_up: null pointer");
+    MB_CHECK_ARG(d % 8 == 0 && h % 8 == 0, "gated_mlp_up: d and h must be multiples of 8");
+    MB_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(out) % 16 == 0,
+                 "gated_mlp_up: pointers must be 16-byte aligned");
+    MB_CHECK_ARG(T <= (int64_t)0x7fffffff - 256 && h <= 0x3fffffff - 256, "gated_mlp_up: too large");
+    if (check_tc_device("gated_mlp_up")) return -1;
+    ProjParams p{};
+    p.M = (int)T;
+    p.N = 2 * h;
+    p.K = d;
+    p.BN = 256;  // 128 gate + 128 up columns -> 128 outputs
+    p.m_tiles = (int)((T + 255) / 256);
+    p.n_tiles = (h + 127) / 128;
+    p.kblocks = (d + kPBK - 1) / kPBK;
+    p.mode = kProjF16;
+    p.halo = 0;
+    p.up_row0 = h;
+    p.idesc = idesc_f16_f32acc(256, 256);
+    p.tx_bytes = (uint32_t)(2 * (kPStageA + kPStageB));
+    CUtensorMap maps[6];
+    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    // The last gate box of an h that is not a multiple of 128 reads up rows:
+    // those columns are beyond h and never stored.
+    const bool enc_ok = encode_2d(&maps[0], F16, 2, x, T, d, d, kPBK, 128) &&
+                        encode_2d(&maps[1], F16, 2, w, 2 * (int64_t)h, d, d, kPBK, 128) &&
+                        encode_2d(&maps[2], F16, 2, out, T, h, h, 64, 32);
+    MB_CHECK_ARG(enc_ok, "gated_mlp_up: tensor map encoding failed");
+    maps[3] = maps[4] = maps[5] = maps[2];
     return launch_proj<false>(maps, p, st);
 }
 

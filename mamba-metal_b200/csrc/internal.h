@@ -66,6 +66,9 @@ unsigned gemm_error_flags(bool clear);
 
 // gemm_tc.cu
 enum ProjMode { kProjF16 = 0, kProjF32Add = 1, kProjF32 = 2 };
+// SwiGLU up-projection on the CTA-pair GEMM: out [T, h] FP16 =
+// silu(x Wg^T) * (x Wu^T), w = [Wg; Wu] FP16 [2h, d] (gate rows first).
+int proj_gemm_gated(const void *x, const void *w_gate_up, void *out, int64_t T, int d, int h, cudaStream_t st);
 int proj_gemm(const void *A, int64_t lda, const void *W, const float *bias, void *C, int64_t ldc, int64_t M, int N,
               int K, int mode, cudaStream_t st);
 constexpr int64_t kProjMinRows = 512;  // mamba_linear uses the CTA-pair GEMM above this many rows
