@@ -121,6 +121,23 @@ int fill_A(float *A, int D, int N, cudaStream_t st) {
     return launch_status("fill_A kernel");
 }
 
+// 1/A per (channel, state), or 0 where |A| <= 1e-6: the same expression the
+// scan and the decode kernels evaluate per CTA, computed once per weight load
+// so the decode state update (read per token) does not divide.
+__global__ void a_inverse_kernel(const float *__restrict__ A, float *__restrict__ Ainv, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float a = A[i];
+        Ainv[i] = fabsf(a) > 1e-6f ? 1.0f / a : 0.f;
+    }
+}
+
+int a_inverse(const float *A, float *Ainv, int64_t n, cudaStream_t st) {
+    if (n <= 0) return 0;
+    a_inverse_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(A, Ainv, n);
+    return launch_status("a_inverse kernel");
+}
+
 int fill_const(float *p, int64_t n, float v, cudaStream_t st) {
     if (n <= 0) return 0;
     fill_const_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(p, n, v);

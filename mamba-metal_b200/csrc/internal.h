@@ -53,7 +53,7 @@ int rmsnorm(const void *x, const float *w, void *y, int64_t rows, int cols, floa
 int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
              const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
              const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
-             int xd, int dd, int bd, cudaStream_t st);
+             int xd, int dd, int bd, cudaStream_t st, const float *A_inv = nullptr);
 unsigned step_error_flags(bool clear);
 
 // carries.cu
@@ -91,6 +91,7 @@ uint64_t fill_key(uint64_t seed, int layer, int tag);
 int fill_random(void *out, int dtype, int64_t n, uint64_t key, int dist, float p0, float p1,
                 cudaStream_t st);
 int fill_A(float *A, int D, int N, cudaStream_t st);
+int a_inverse(const float *A, float *Ainv, int64_t n, cudaStream_t st);
 int fill_const(float *p, int64_t n, float v, cudaStream_t st);
 int transpose_cast(const float *src, void *dst, int dtype, int K, int N, cudaStream_t st);
 int untranspose_widen(const void *src, float *dst, int dtype, int K, int N, cudaStream_t st);

@@ -134,6 +134,7 @@ struct LayerWeights {
     float *conv_w = nullptr;  // [D, K]
     float *conv_b = nullptr;  // [D]
     float *A = nullptr;       // [D, N]
+    float *A_inv = nullptr;   // [D, N] 1/A (0 where |A| <= 1e-6), derived at load
     float *Dskip = nullptr;   // [D]
     float *norm_w = nullptr;  // [M]
     float *dt_bias = nullptr; // [D]
@@ -299,6 +300,7 @@ struct Model {
         s += align_up((size_t)D * K * 4);
         s += align_up((size_t)D * 4);
         s += align_up((size_t)D * N * 4);
+        s += align_up((size_t)D * N * 4);  // A_inv
         s += align_up((size_t)D * 4);
         s += align_up((size_t)M * 4);
         s += align_up((size_t)D * 4);
@@ -361,6 +363,7 @@ struct Model {
             w.conv_w = reinterpret_cast<float *>(take((size_t)D * K * 4));
             w.conv_b = reinterpret_cast<float *>(take((size_t)D * 4));
             w.A = reinterpret_cast<float *>(take((size_t)D * N * 4));
+            w.A_inv = reinterpret_cast<float *>(take((size_t)D * N * 4));
             w.Dskip = reinterpret_cast<float *>(take((size_t)D * 4));
             w.norm_w = reinterpret_cast<float *>(take((size_t)M * 4));
             w.dt_bias = reinterpret_cast<float *>(take((size_t)D * 4));
@@ -864,7 +867,7 @@ static int step_enqueue(Model &m, MambaStateHandle &s, const float *tok, float *
             const char *xdbc = static_cast<const char *>(ar.xdbc);
             if (ssm_step(ar.u, D, ar.draw, D, w.dt_bias, xdbc + (size_t)R * a, xdbc + (size_t)(R + N) * a, XD,
                          w.A, w.Dskip, static_cast<const char *>(ar.xz) + (size_t)D * a, 2 * D, ar.y, D,
-                         ssm_state, Bt, D, N, m.act, m.act, m.act, st))
+                         ssm_state, Bt, D, N, m.act, m.act, m.act, st, w.A_inv))
                 return -1;
         }
         {
@@ -1007,6 +1010,7 @@ static int load_weights(Model &m, const void *data, size_t size) {
         if (transpose_cast(s, w.w_dt_t, m.act, R, D, st)) return -1;
         s += (size_t)R * D;
         MB_CUDA_TRY(cudaMemcpyAsync(w.A, s, (size_t)D * N * 4, cudaMemcpyDeviceToDevice, st));
+        if (a_inverse(w.A, w.A_inv, (int64_t)D * N, st)) return -1;
         s += (size_t)D * N;
         MB_CUDA_TRY(cudaMemcpyAsync(w.Dskip, s, (size_t)D * 4, cudaMemcpyDeviceToDevice, st));
         s += D;
@@ -1086,6 +1090,7 @@ static int init_random(Model &m, uint64_t seed) {
         if (fill_random(w.w_out_t, m.act, (int64_t)M * D, fill_key(seed, l, kTagOut), 0, 0.f, 0.02f, st)) return -1;
         if (fill_random(w.dt_bias, MAMBA_F32, D, fill_key(seed, l, kTagDtBias), 2, 1e-3f, 1e-1f, st)) return -1;
         if (fill_A(w.A, D, N, st)) return -1;
+        if (a_inverse(w.A, w.A_inv, (int64_t)D * N, st)) return -1;
         if (fill_const(w.Dskip, D, 1.f, st)) return -1;
         if (fill_const(w.norm_w, M, 1.f, st)) return -1;
     }

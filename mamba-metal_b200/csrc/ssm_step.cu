@@ -223,7 +223,8 @@ __global__ void __launch_bounds__(128, 12)
                          const float *__restrict__ dt_bias, const Tbc *__restrict__ Bm,
                          const Tbc *__restrict__ Cm, int64_t bcrs, const float *__restrict__ A,
                          const float *__restrict__ Dskip, const Tx *__restrict__ z, int64_t zrs,
-                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int batch, int D) {
+                         Tx *__restrict__ y, int64_t yrs, float *__restrict__ state, int batch, int D,
+                         const float *__restrict__ A_inv) {
     constexpr int NS = 16, S = 4, kRowFloats = 32 * NS;  // one row's state run: 32 channels x 16 states
     extern __shared__ __align__(128) unsigned char smem[];
     float *sst = reinterpret_cast<float *>(smem);  // [RB][32][16]
@@ -252,10 +253,18 @@ __global__ void __launch_bounds__(128, 12)
     const float4 a4 = *reinterpret_cast<const float4 *>(A + (int64_t)d * NS + q * S);
     const float av[4] = {a4.x, a4.y, a4.z, a4.w};
     float ac[S], kI[S];
+    if (A_inv) {
+        // precomputed by the model at weight load (same expression, same bits)
+        const float4 k4 = *reinterpret_cast<const float4 *>(A_inv + (int64_t)d * NS + q * S);
+        kI[0] = k4.x;
+        kI[1] = k4.y;
+        kI[2] = k4.z;
+        kI[3] = k4.w;
+    }
 #pragma unroll
     for (int j = 0; j < S; ++j) {
         ac[j] = av[j] * kLog2e;
-        kI[j] = fabsf(av[j]) > 1e-6f ? 1.0f / av[j] : 0.f;
+        if (!A_inv) kI[j] = fabsf(av[j]) > 1e-6f ? 1.0f / av[j] : 0.f;
     }
     const float bias = dt_bias ? dt_bias[d] : 0.f;
     const float dsk = Dskip ? Dskip[d] : 0.f;
@@ -324,7 +333,7 @@ template <int NS, typename Tx, typename Tdt, typename Tbc>
 int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
                 const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
                 const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
-                int N, cudaStream_t st) {
+                int N, cudaStream_t st, const float *A_inv) {
     const int aligned = reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(state) % 16 == 0;
     if (!std::is_same<Tx, float>::value) {
         // Four threads per channel, 32 channels per CTA, R batch rows per
@@ -341,7 +350,8 @@ int launch_step(const void *x, int64_t xrs, const void *delta, int64_t drs, cons
             ssm_step_bulk_kernel<RB, Tx, Tdt, Tbc><<<grid, 128, smem, st>>>(
                 static_cast<const Tx *>(x), xrs, static_cast<const Tdt *>(delta), drs, dt_bias,
                 static_cast<const Tbc *>(B), static_cast<const Tbc *>(C), bcrs, A, Dskip,
-                static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, batch, D);
+                static_cast<const Tx *>(z), zrs, static_cast<Tx *>(y), yrs, state, batch, D,
+                A_inv && reinterpret_cast<uintptr_t>(A_inv) % 16 == 0 ? A_inv : nullptr);
             return launch_status("ssm_step (bulk copies) kernel");
         }
         const bool many = (int64_t)ceil_div(D, 32) * ceil_div(batch, R) >= 2LL * device_sm_count();
@@ -372,15 +382,15 @@ template <typename Tx, typename Tdt, typename Tbc>
 int launch_step_ns(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
                    const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
                    const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D,
-                   int N, cudaStream_t st) {
+                   int N, cudaStream_t st, const float *A_inv) {
     if (N <= 4)
         return launch_step<4, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
-                                            yrs, state, batch, D, N, st);
+                                            yrs, state, batch, D, N, st, A_inv);
     if (N <= 8)
         return launch_step<8, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
-                                            yrs, state, batch, D, N, st);
+                                            yrs, state, batch, D, N, st, A_inv);
     return launch_step<16, Tx, Tdt, Tbc>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs, y,
-                                         yrs, state, batch, D, N, st);
+                                         yrs, state, batch, D, N, st, A_inv);
 }
 
 }  // namespace
@@ -388,7 +398,7 @@ int launch_step_ns(const void *x, int64_t xrs, const void *delta, int64_t drs, c
 int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const float *dt_bias,
              const void *B, const void *C, int64_t bcrs, const float *A, const float *Dskip,
              const void *z, int64_t zrs, void *y, int64_t yrs, float *state, int batch, int D, int N,
-             int xd, int dd, int bd, cudaStream_t st) {
+             int xd, int dd, int bd, cudaStream_t st, const float *A_inv) {
     MB_CHECK_ARG(batch >= 0 && D >= 0, "ssm_step: negative size");
     MB_CHECK_ARG(N >= 1 && N <= 16, "ssm_step: dstate must be in 1..16");
     MB_CHECK_ARG(batch <= 65535, "ssm_step: batch > 65535");
@@ -396,16 +406,16 @@ int ssm_step(const void *x, int64_t xrs, const void *delta, int64_t drs, const f
     MB_CHECK_ARG(x && delta && B && C && A && y && state, "ssm_step: null pointer");
     if (xd == MAMBA_F32 && dd == MAMBA_F32 && bd == MAMBA_F32)
         return launch_step_ns<float, float, float>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z, zrs,
-                                                   y, yrs, state, batch, D, N, st);
+                                                   y, yrs, state, batch, D, N, st, A_inv);
     if (xd == MAMBA_F16 && dd == MAMBA_F16 && bd == MAMBA_F16)
         return launch_step_ns<__half, __half, __half>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
-                                                      zrs, y, yrs, state, batch, D, N, st);
+                                                      zrs, y, yrs, state, batch, D, N, st, A_inv);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F16)
         return launch_step_ns<__half, float, __half>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
-                                                     zrs, y, yrs, state, batch, D, N, st);
+                                                     zrs, y, yrs, state, batch, D, N, st, A_inv);
     if (xd == MAMBA_F16 && dd == MAMBA_F32 && bd == MAMBA_F32)
         return launch_step_ns<__half, float, float>(x, xrs, delta, drs, dt_bias, B, C, bcrs, A, Dskip, z,
-                                                    zrs, y, yrs, state, batch, D, N, st);
+                                                    zrs, y, yrs, state, batch, D, N, st, A_inv);
     set_error("ssm_step: unsupported dtype combination");
     return -1;
 }
