@@ -268,15 +268,20 @@ __global__ void __launch_bounds__(128, 12)
     }
     const float bias = dt_bias ? dt_bias[d] : 0.f;
     const float dsk = Dskip ? Dskip[d] : 0.f;
-    float xv[RB], draw[RB], zv[RB];
+    // Lane q of a channel's quad evaluates softplus(delta) and SiLU(z) of
+    // row q only (one each instead of four); the rows' dt values reach the
+    // other lanes by shuffle, and lane q writes row q's output.
+    static_assert(RB <= 4, "one row per lane of the quad");
+    float xv[RB];
 #pragma unroll
-    for (int r = 0; r < RB; ++r) {
-        const int b = b0 + (r < nr ? r : 0);
-        xv[r] = ld_f32(x + (int64_t)b * xrs + d);
-        draw[r] = ld_f32(delta + (int64_t)b * drs + d);
-        zv[r] = (z && q == 0) ? ld_f32(z + (int64_t)b * zrs + d) : 0.f;
-    }
+    for (int r = 0; r < RB; ++r) xv[r] = ld_f32(x + (int64_t)(b0 + (r < nr ? r : 0)) * xrs + d);
+    const int bq = b0 + (q < nr ? q : 0);
+    const float draw_q = ld_f32(delta + (int64_t)bq * drs + d);
+    const float zq = z ? ld_f32(z + (int64_t)bq * zrs + d) : 0.f;
     __syncthreads();  // sBC
+    const float dt_q = softplus_fast(dt_bias ? __fadd_rn(draw_q, bias) : draw_q);
+    const float gate_q = z ? silu_fast(zq) : 1.f;
+    const int quad0 = (tid & 31) & ~3;
     bool ok = true;
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
@@ -289,7 +294,7 @@ __global__ void __launch_bounds__(128, 12)
         float *hp = sst + r * kRowFloats + cl * NS + q * S;
         const float4 hv = *reinterpret_cast<const float4 *>(hp);
         float h[S] = {hv.x, hv.y, hv.z, hv.w};
-        const float dt = softplus_fast(dt_bias ? __fadd_rn(draw[r], bias) : draw[r]);
+        const float dt = __shfl_sync(0xffffffffu, dt_q, quad0 + r);
         const float *bc = sBC + r * 2 * NS;
         float yp = 0.f;
 #pragma unroll
@@ -302,10 +307,7 @@ __global__ void __launch_bounds__(128, 12)
         *reinterpret_cast<float4 *>(hp) = make_float4(h[0], h[1], h[2], h[3]);
         yp += __shfl_xor_sync(0xffffffffu, yp, 1);
         yp += __shfl_xor_sync(0xffffffffu, yp, 2);
-        if (q == 0) {
-            const float gate = z ? silu_fast(zv[r]) : 1.f;
-            y[(int64_t)(b0 + r) * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv[r], yp) * gate);
-        }
+        if (q == r) y[(int64_t)(b0 + r) * yrs + d] = cvt_out<Tx>(fmaf(dsk, xv[r], yp) * gate_q);
     }
     fence_proxy_async_smem();  // the updated rows are read by the bulk stores
     const bool aborted = __syncthreads_or(!ok);
