@@ -72,7 +72,9 @@ __global__ void conv1d_step_kernel(const T *__restrict__ x, int64_t xrs, const f
 #pragma unroll
     for (int k = 0; k < K; ++k) acc = fmaf(win[k], w[(int64_t)d * K + k], acc);
     if (bias) acc += bias[d];
-    if (silu) acc = silu_f(acc);
+    // FP16 activations: the full-sequence kernel's SiLU (one ex2 + Newton
+    // reciprocal), so decode and forward apply the same function
+    if (silu) acc = sizeof(T) == 4 ? silu_f(acc) : silu_fast(acc);
     y[(int64_t)b * yrs + d] = cvt_out<T>(acc);
 #pragma unroll
     for (int k = 0; k < K - 1; ++k) st[k] = win[k + 1];
