@@ -100,11 +100,12 @@ const char *mamba_last_error(void);
 /* Error flags raised by kernels on the current device since the last
  * clear (0 = none).  Bit 0: a shared-memory pipeline wait inside the
  * selective scan exceeded its 2-second bound, so that call stopped early and
- * its outputs are invalid.  Bit 1: the same for a wait inside
- * mamba_gated_mlp_up.  Bit 2: the same for mamba_linear (and the decode
- * projections that use it).  Bit 3: set by mamba_selftest_bounded_wait.
- * Bit 4: the same as bit 0 for the CTA-pair projection GEMM (the model's
- * forward projections, mamba_linear above 512 rows).  Bit 5: the same for
+ * its outputs are invalid.  Bit 1: the same for a wait inside the one-CTA
+ * SwiGLU kernel (mamba_gated_mlp_up with MAMBA_MLP_PAIR=0).  Bit 2: the same
+ * for mamba_linear (and the decode projections that use it).  Bit 3: set by
+ * mamba_selftest_bounded_wait.  Bit 4: the same as bit 0 for the CTA-pair
+ * projection GEMM (the model's forward projections, mamba_linear above 512
+ * rows, mamba_gated_mlp_up by default).  Bit 5: the same for
  * the decode state update's bulk-copy waits (mamba_ssm_step, mamba_step).
  * Waits for the device; clear != 0 resets them. */
 unsigned mamba_device_status(int clear);
@@ -428,7 +429,9 @@ int mamba_in_proj_conv(const void *x, const void *w_in, const float *conv_w, con
  * 0..h-1 and w_up in rows h..2h-1 (the nn.Linear weight layout); out FP16
  * [tokens, h].  FP32 accumulation; the gate is applied to the FP32
  * accumulators and rounded once.  d and h multiples of 8, pointers 16-byte
- * aligned.  Needs a compute capability 10.x GPU. */
+ * aligned.  Needs a compute capability 10.x GPU.  Runs on the CTA-pair
+ * projection GEMM (gate rows in one CTA of the pair, the matching up rows in
+ * the other); MAMBA_MLP_PAIR=0 selects the one-CTA kernel instead. */
 int mamba_gated_mlp_up(const void *x, const void *w_gate_up, void *out, int64_t tokens, int d, int h,
                        void *stream);
 
